@@ -1,0 +1,446 @@
+"""Benchmark of the denoiser self-attention path (BASELINE.json metric: Sage attention ms/call and TOPS at 16.8k / 47k
+tokens, % of the int8 tensor peak, 1/2/4/8 GPUs).
+
+One step = one h3s_attention call of the 47,232-token case (c3: 32 heads x 128, fp16 q/k/v as the strided parts of a
+qkv buffer, fp16 out), with a fresh seeded input per denoiser block (50 blocks, each > L2). With N GPUs (torchrun), the
+32 heads are split over the ranks (32/N heads each, no exchange: heads are independent), so the total work is fixed
+(strong scaling). Also reported: c2 (16,848 tokens, Sage), c1 (2,159 tokens, fp16 SDPA) and, for N > 1, the Ulysses
+variant c4 (token-sharded activations, NCCL all-to-all to head shards and back) with its exposed all-to-all time.
+
+--impl reference times the reference's attention restated on the CPU (oracle/, the reference itself cannot be built
+here) on the host cores, rank 0 only, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "Sage attn ms/call & TOPS at 16.8k/47k tokens, % int8 TC peak, 1/2/4/8 GPU"
+UNIT = "TOPS"
+DATA = ("synthetic: seeded N(0,1) q and v, k = N(0,1) + a per-channel N(0,4) offset, fresh per block "
+        "(no dataset; stands in for the denoiser's activations)")
+
+
+def ops_per_call(S: int, H: int, D: int = 128) -> float:
+    """Algorithmic work of one attention call: Q.K^T and P.V, 2*S*S*D*H each."""
+    return 4.0 * S * S * D * H
+
+
+def measured_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class Clocks:
+    """nvidia-smi samples of the SM clock and throttle reasons while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.rows: list[list[str]] = []
+        self.proc = None
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self) -> dict:
+        sm = [float(r[0]) for r in self.rows if len(r) >= 6 and r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if len(r) >= 6 and r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) >= 6 for i in range(4) if r[2 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# CPU side: the oracle (the reference's attention restated; oracle/sage_ref.cpp)
+# ---------------------------------------------------------------------------------------------------------------------
+def cpu_sage_tops(S: int, H: int, D: int, budget_s: float, seed: int = 1) -> dict:
+    """Times the oracle's Sage path on this host: the whole pre-pass on the full input, then a sample of query rows
+    (spread over heads and positions) through the int8 attention; the call time is the pre-pass plus the rows' time
+    scaled by the exact work ratio (every row costs 4*S*D ops)."""
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    from sycl_minimax_h3_b200.workloads import bits, make_qkv
+
+    oracle.build()
+    host = bits(make_qkv(S, H, D, seed=seed))
+    st = 3 * H * D
+    t0 = time.perf_counter()
+    iq, ik, qs, ks, km, hv = oracle.sage_prepass(host, (host, H * D), (host, 2 * H * D), oracle.F16, S, H, D, st)
+    t_pre = time.perf_counter() - t0
+    rng = np.random.default_rng(seed)
+    n = max(8, oracle.threads())
+    t_rows, done = 0.0, 0
+    while True:
+        rh = rng.integers(0, H, n)
+        rs = rng.integers(0, S, n)
+        t0 = time.perf_counter()
+        oracle.sage_rows(iq, ik, hv, qs, ks, S, H, D, rh, rs)
+        t_rows += time.perf_counter() - t0
+        done += n
+        if t_rows + t_pre >= budget_s or done >= H * S:
+            break
+        n = min(H * S - done, max(n, int(n * (budget_s - t_pre - t_rows) / max(t_rows, 1e-3))))
+    t_call = t_pre + t_rows * (H * S) / done
+    return {"value": ops_per_call(S, H, D) / t_call / 1e12, "unit": UNIT, "cores": oracle.threads(), "kind": "port",
+            "sample": f"S={S}, H={H}: full pre-pass ({t_pre:.2f} s) + {done} of {H * S} query rows ({t_rows:.2f} s), "
+                      f"scaled to a whole call = {t_call:.1f} s",
+            "s_per_call": t_call}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    S, H, D = 47232, 32, 128
+    per_step = []
+    budget = float(os.environ.get("H3_REF_STEP_S", "10"))
+    for i in range(args.warmup + args.steps):
+        r = cpu_sage_tops(S, H, D, budget_s=budget if i >= args.warmup else 2.0, seed=100 + i)
+        if i >= args.warmup:
+            per_step.append(r)
+    tops = statistics.median(r["value"] for r in per_step)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tops, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * statistics.median(r["s_per_call"] for r in per_step),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8+fp16", "data": DATA,
+        "config": {"workload": "c3: 32 heads x 47,232 tokens x 128, Sage path, fp16 in/out", "S": S, "H": H, "D": D},
+        "cpu_baseline": {k: per_step[-1][k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": tops, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's own attention (SYCL + oneDNN + un-vendored ARK) cannot be built or run here; this is "
+                "its algorithm restated in C++ (oracle/sage_ref.cpp) on the host cores",
+    }
+    line["cpu_baseline"]["value"] = tops
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# GPU side
+# ---------------------------------------------------------------------------------------------------------------------
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--quick", action="store_true", help="main workload only (no c1/c2/c4 side numbers)")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from sycl_minimax_h3_b200 import native, ops
+    from sycl_minimax_h3_b200.workloads import make_qkv
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    peaks = measured_peaks()
+    D = 128
+    S, H = 47232, 32
+    if H % world:
+        raise SystemExit(f"{H} heads do not split over {world} GPUs")
+    h = H // world
+    nblocks = 50
+    stream = torch.cuda.current_stream()
+    ctx = ops.context(dev)
+
+    # ---- inputs: a fresh seeded qkv per denoiser block, this rank's heads ----
+    pool = []
+    for b in range(min(nblocks, args.warmup + args.steps)):
+        g = torch.Generator(device=dev)
+        g.manual_seed(1000 + b)
+        qkv = torch.randn(S, 3 * H * D, generator=g, device=dev, dtype=torch.float16)
+        off = torch.randn(H * D, generator=g, device=dev, dtype=torch.float32) * 2.0
+        qkv[:, H * D:2 * H * D] += off.to(torch.float16)
+        pool.append(qkv.view(S, 3, H, D)[:, :, rank * h:(rank + 1) * h, :].reshape(S, 3 * h * D).contiguous())
+        del qkv
+    out = torch.empty(S, h * D, dtype=torch.float16, device=dev)
+    torch.cuda.synchronize()
+
+    def call(qkv):
+        q, k, v = ops.Rows.qkv(qkv, h, D)
+        ops.attention(q, k, v, out)
+
+    # ---- timed region: K calls, one per block ----
+    for i in range(args.warmup):
+        call(pool[i % len(pool)])
+    ctx.wait()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record(stream)
+        for i in range(args.steps):
+            call(pool[(args.warmup + i) % len(pool)])
+        e1.record(stream)
+        torch.cuda.synchronize()
+    ctx.wait()
+    barrier()
+    ms_total = max_over_ranks(e0.elapsed_time(e1))
+    ms_call = ms_total / args.steps
+    value = ops_per_call(S, H, D) * args.steps / (ms_total / 1e3) / 1e12
+    launches_per_call = 4  # K mean, Q quantiser, K quantiser, attention
+
+    # ---- the dominant kernel alone: attention on quantised inputs, through the plugin's C ABI ----
+    nb = (S + 63) // 64
+    iq = torch.empty(h, S, D, dtype=torch.int8, device=dev)
+    ik = torch.empty_like(iq)
+    sc = torch.empty(2 * h * nb + h * D, dtype=torch.float32, device=dev)
+    ctx.sage_prepass(pool[0].data_ptr(), pool[0].data_ptr() + h * D * 2, native.F16, S, h, D, 3 * h * D, iq.data_ptr(),
+                     ik.data_ptr(), sc.data_ptr())
+    ctx.wait()
+    sage = native.sage_lib()
+    import ctypes
+
+    raw = ctypes.c_void_p(stream.cuda_stream)
+    vptr = pool[0].data_ptr() + 2 * h * D * 2
+
+    def kernel_only():
+        rc = sage.h3sage_attention_strided(ctypes.byref(raw), iq.data_ptr(), ik.data_ptr(), vptr, 3 * h * D, D,
+                                           out.data_ptr(), native.F16, h * D, D, sc.data_ptr(),
+                                           sc.data_ptr() + h * nb * 4, 64, S, h, D, 1.0 / D ** 0.5, None, 0)
+        if rc != 0:
+            raise native.H3Error(sage.h3sage_error().decode())
+
+    for _ in range(3):
+        kernel_only()
+    torch.cuda.synchronize()
+    nk = max(5, min(20, args.steps))
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    k0.record(stream)
+    for _ in range(nk):
+        kernel_only()
+    k1.record(stream)
+    torch.cuda.synchronize()
+    if sage.h3sage_check(ctypes.byref(raw)) != 0:
+        raise native.H3Error(sage.h3sage_error().decode())
+    ms_kernel = k0.elapsed_time(k1) / nk
+    mixed_peak = 4.0 / 3.0 * peaks["bf16_tflops"]          # half the ops int8 at 2x the bf16 rate, half fp16
+    achieved = ops_per_call(S, h, D) / (ms_kernel / 1e3) / 1e12
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": mixed_peak, "unit": "TFLOP/s",
+                "frac": achieved / mixed_peak, "traffic": None,
+                "kernel": "attn_fwd<true> (Sage int8 QK^T + fp16 PV, tcgen05)",
+                "peak_basis": f"4/3 x {peaks['source']} bf16 {peaks['bf16_tflops']} TFLOP/s: int8 QK^T at 2x, fp16 PV at 1x",
+                "ms_per_launch": ms_kernel,
+                "pct_int8_peak_measured_x2": achieved / (2 * peaks["bf16_tflops"]),
+                "pct_int8_peak_nominal_4500": achieved / 4500.0}
+
+    # ---- pre-pass alone: HBM-bound ----
+    for _ in range(2):
+        ctx.sage_prepass(pool[1 % len(pool)].data_ptr(), pool[1 % len(pool)].data_ptr() + h * D * 2, native.F16, S, h, D,
+                         3 * h * D, iq.data_ptr(), ik.data_ptr(), sc.data_ptr())
+    torch.cuda.synchronize()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record(stream)
+    npre = 5
+    for i in range(npre):
+        blk = pool[(2 + i) % len(pool)]
+        ctx.sage_prepass(blk.data_ptr(), blk.data_ptr() + h * D * 2, native.F16, S, h, D, 3 * h * D, iq.data_ptr(),
+                         ik.data_ptr(), sc.data_ptr())
+    p1.record(stream)
+    torch.cuda.synchronize()
+    ctx.wait()
+    ms_pre = p0.elapsed_time(p1) / npre
+    pre_bytes = 6.0 * S * h * D + 4 * h * D + 8 * h * nb     # read q, k (fp16), write int8 q, k, scales and means
+    prepass = {"ms": ms_pre, "algorithmic_GBs": pre_bytes / (ms_pre / 1e3) / 1e9,
+               "with_mean_reread_GBs": (pre_bytes + 2.0 * S * h * D) / (ms_pre / 1e3) / 1e9,
+               "peak_hbm_GBs": peaks["hbm_gbs"]}
+
+    # ---- end to end: host buffers through the public call, H2D of the inputs and D2H of the output every step ----
+    ne = min(args.steps, 10)
+    host_in = [pool[i % len(pool)].cpu().pin_memory() for i in range(2)]
+    host_out = torch.empty(S, h * D, dtype=torch.float16).pin_memory()
+    dev_in = torch.empty_like(pool[0])
+    for i in range(2):
+        dev_in.copy_(host_in[i], non_blocking=True)
+        call(dev_in)
+        host_out.copy_(out, non_blocking=True)
+    torch.cuda.synchronize()
+    barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(ne):
+        dev_in.copy_(host_in[i % 2], non_blocking=True)
+        call(dev_in)
+        host_out.copy_(out, non_blocking=True)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ctx.wait()
+    barrier()
+    ms_e2e = max_over_ranks(t0.elapsed_time(t1)) / ne
+    e2e = {"value": ops_per_call(S, H, D) / (ms_e2e / 1e3) / 1e12, "unit": UNIT,
+           "h2d_bytes_per_step": int(dev_in.numel() * 2) * world, "d2h_bytes_per_step": int(out.numel() * 2) * world,
+           "ms_per_step": ms_e2e}
+    del host_in, host_out, dev_in
+
+    extra = {}
+    if not args.quick:
+        # c2: 16,848 tokens, Sage; c1: 2,159 tokens, fp16 SDPA (heads split the same way)
+        for name, S2, sage_path in (("c2", 16848, True), ("c1", 2159, False)):
+            qkv2 = make_qkv(S2, h, D, seed=77, device=dev)
+            out2 = torch.empty(S2, h * D, dtype=torch.float16, device=dev)
+            if not sage_path:
+                os.environ["H3S_SAGE_MIN_S"] = str(1 << 30)
+                ops._ctx.clear()
+            q2, k2, v2 = ops.Rows.qkv(qkv2, h, D)
+            for _ in range(3):
+                ops.attention(q2, k2, v2, out2)
+            torch.cuda.synchronize()
+            barrier()
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            nrep = 20
+            a0.record(torch.cuda.current_stream())
+            for _ in range(nrep):
+                ops.attention(q2, k2, v2, out2)
+            a1.record(torch.cuda.current_stream())
+            torch.cuda.synchronize()
+            ops.context(dev).wait()
+            barrier()
+            ms2 = max_over_ranks(a0.elapsed_time(a1)) / nrep
+            extra[name] = {"S": S2, "H": H, "ms_per_call": ms2, "tops": ops_per_call(S2, H, D) / (ms2 / 1e3) / 1e12,
+                           "path": "sage" if sage_path else "fp16 sdpa"}
+            if not sage_path:
+                os.environ.pop("H3S_SAGE_MIN_S", None)
+                ops._ctx.clear()
+            del qkv2, out2
+        if world > 1:
+            extra["c4_ulysses"] = ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_sage_tops(S, H, D, budget_s=float(os.environ.get("H3_CPU_BUDGET_S", "15")))
+        cpu.pop("s_per_call", None)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_call, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int8+fp16", "data": DATA,
+            "config": {"workload": "c3: 32 heads x 47,232 tokens x 128 per call, Sage path, fp16 q/k/v inside a qkv buffer "
+                                   "(row stride 3*H*D), fp16 out; 50 fresh blocks",
+                       "S": S, "H": H, "D": D, "blocks": min(nblocks, args.warmup + args.steps),
+                       "parallelism": f"heads/{world}" if world > 1 else "1 GPU",
+                       "l2": "inputs larger than L2 (1.16 GB per block), a different block every step"},
+            "ms_per_call": ms_call, "pct_int8_peak_measured_x2": value / world / (2 * peaks["bf16_tflops"]),
+            "roofline": roofline, "prepass": prepass, "e2e": e2e, "gpu_launches": launches_per_call * args.steps,
+            "clocks": clk.summary(), "extra": extra,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier) -> dict:
+    """c4: token-sharded qkv -> all-to-all -> attention of H/P heads over all S tokens -> inverse all-to-all."""
+    import torch
+
+    from sycl_minimax_h3_b200 import ops, ulysses
+
+    s = S // world
+    g = torch.Generator(device=dev)
+    g.manual_seed(5000 + rank)
+    shard = torch.randn(s, 3 * H * D, generator=g, device=dev, dtype=torch.float16)
+    h = H // world
+    out = torch.empty(S, h * D, dtype=torch.float16, device=dev)
+
+    def step(times=None):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        ev[0].record()
+        qkv_heads = ulysses.seq_to_heads(shard, H, D)
+        ev[1].record()
+        q, k, v = ops.Rows.qkv(qkv_heads, h, D)
+        ops.attention(q, k, v, out)
+        ev[2].record()
+        res = ulysses.heads_to_seq(out, H, D)
+        ev[3].record()
+        if times is not None:
+            times.append(ev)
+        return res
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    times = []
+    n = 10
+    for _ in range(n):
+        step(times)
+    torch.cuda.synchronize()
+    ops.context(dev).wait()
+    a2a = sum(e[0].elapsed_time(e[1]) + e[2].elapsed_time(e[3]) for e in times) / n
+    att = sum(e[1].elapsed_time(e[2]) for e in times) / n
+    tot = sum(e[0].elapsed_time(e[3]) for e in times) / n
+    return {"tokens_per_gpu": s, "heads_per_gpu": h, "ms_per_call": max_over_ranks(tot),
+            "ms_all_to_all_exposed": max_over_ranks(a2a), "ms_attention": max_over_ranks(att),
+            "tops": ops_per_call(S, H, D) / (max_over_ranks(tot) / 1e3) / 1e12}
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,115 @@
+/* h3cuda.h - the C ABI of libh3cuda.so: the denoiser self-attention path of MiniMax H3 on NVIDIA B200 (sm_100a).
+ *
+ * A drop-in for the attention subset of the reference's kernels/h3sycl.h (maxfridbe/sycl_minimax_h3): the same names,
+ * signatures, element-type codes and error conventions, with SYCL queues replaced by CUDA streams and USM by cudaMalloc.
+ * Each declaration cites the reference declaration it replaces (file:line inside the reference project).
+ *
+ * Every data pointer is a device pointer of the context's GPU. Kernels are asynchronous: a call returns once its work
+ * is queued on the context's stream, and the stream is in order, so a later call sees an earlier call's result;
+ * h3s_read and h3s_wait are the points that wait. Functions returning int give 0, or -1 with the reason in
+ * h3s_last_error() (per thread). Functions returning a pointer give NULL on failure, same.
+ *
+ * Environment (read when a context is made; same meanings as the reference's, kernels/h3sycl.cpp:216-235):
+ *   H3S_ATTN=onednn (or =sdpa)  never use the int8 Sage path
+ *   H3S_SAGE_MIN_S             sequences at least this long use Sage (default 8192)
+ *   H3S_MEM_FRACTION           allocation cap as a fraction of the card (default 0.94)
+ *   H3S_PROFILE                wait after every attention phase and report its time on stderr
+ *   H3S_POISON                 fill new buffers with 0xff bytes (NaN) to expose reads of unwritten memory
+ *   H3S_WAIT_MS                limit of every wait inside a kernel (default 2000); past it the kernel stops and
+ *                              h3s_wait reports the failure
+ */
+#ifndef H3CUDA_H
+#define H3CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types of floating-point tensors (kernels/h3sycl.h:21) */
+enum { H3S_F32 = 0, H3S_F16 = 1, H3S_BF16 = 2 };
+
+/* kernels/h3sycl.h:23 */
+const char* h3s_last_error(void);
+
+/* ---- context ---------------------------------------------------------------------------------------------------- */
+
+/* A context on the first GPU with its own stream (kernels/h3sycl.h:28). */
+void* h3s_open(void);
+/* The GPUs CUDA sees; name, memory size and PCI address "0000:0b:00.0" of one (kernels/h3sycl.h:31-32). */
+int h3s_gpu_count(void);
+int h3s_gpu_info(int index, char* name, int name_len, uint64_t* mem_bytes, char* pci, int pci_len);
+/* A context on GPU `index` with its own stream (kernels/h3sycl.h:33). */
+void* h3s_open_gpu(int index);
+/* A context around an existing stream: `stream` points to a cudaStream_t (PyTorch: the handle of
+ * torch.cuda.current_stream()), which is copied; the current device is the context's GPU (kernels/h3sycl.h:36). */
+void* h3s_create(void* stream);
+/* Waits for the stream, frees the scratch buffers and everything still allocated with h3s_alloc (kernels/h3sycl.h:38). */
+void h3s_destroy(void* ctx);
+/* kernels/h3sycl.h:40 */
+const char* h3s_device_name(void* ctx);
+
+/* ---- device memory (kernels/h3sycl.h:47-53) --------------------------------------------------------------------- */
+
+/* Allocations are counted, and one that would pass the cap (0.94 of the card; H3S_MEM_FRACTION overrides) is refused
+ * with an error. The attention's own scratch buffers count against the same cap. */
+void* h3s_alloc(void* ctx, uint64_t bytes);
+void h3s_free(void* ctx, void* p); /* waits for the stream first */
+uint64_t h3s_mem_used(void* ctx);
+uint64_t h3s_mem_cap(void* ctx);
+/* What the whole card has free right now, every process counted. */
+uint64_t h3s_mem_free(void* ctx);
+
+/* ---- copies (kernels/h3sycl.h:56-61) ---------------------------------------------------------------------------- */
+
+/* Host <-> device; both wait for the copy (and for the work queued before it). Thread-safe. */
+int h3s_write(void* ctx, void* dst, const void* src_host, uint64_t bytes);
+int h3s_read(void* ctx, void* dst_host, const void* src, uint64_t bytes);
+/* Device to device, queued like a kernel. */
+int h3s_copy(void* ctx, void* dst, const void* src, uint64_t bytes);
+/* Waits until everything queued has run; reports an asynchronous error (a CUDA error, or a kernel wait that gave up). */
+int h3s_wait(void* ctx);
+
+/* ---- pinned host memory and uploads beside the kernels (kernels/h3sycl.h:65-71) --------------------------------- */
+
+void* h3s_alloc_host(void* ctx, uint64_t bytes);
+void h3s_free_host(void* ctx, void* p); /* waits for the uploads first */
+/* Pinned host -> device on the context's copy stream; the kernels do not wait for it: call h3s_upload_wait before
+ * using dst. src must come from h3s_alloc_host, dst must be device memory; anything else is refused. */
+int h3s_upload(void* ctx, void* dst, const void* src_pinned, uint64_t bytes);
+int h3s_upload_wait(void* ctx);
+
+/* ---- attention (kernels/h3sycl.h:185-197) ----------------------------------------------------------------------- */
+
+/* out = softmax(q . k^T / sqrt(D)) . v, per head. q, k, v: S token rows of H heads x D features, row s at element
+ * s * stride (stride >= H * D; 3 * H * D when they sit inside the qkv linear's output), in type dt; out [S, H * D] in
+ * out_dt, rounded through half. S >= H3S_SAGE_MIN_S (8192): SageAttention v1 (int8 q, k with per-64-row scales after
+ * k's channel mean is taken out; libh3sage.so beside this library); shorter: fp16 SDPA. D = 128. S, H or D <= 0:
+ * nothing to do, returns 0. No score table is ever written: memory stays O(S * H * D). (kernels/h3sycl.h:190-191) */
+int h3s_attention(void* ctx, const void* q, const void* k, const void* v, int dt, int64_t S, int64_t H, int64_t D,
+                  int64_t stride, void* out, int out_dt);
+/* B independent sequences of S tokens in one call: sequence b's rows start at row b * S of q, k, v and of out
+ * [B * S, H * D]. Below the Sage threshold all sequences go in one launch; Sage takes them one at a time.
+ * (kernels/h3sycl.h:196-197) */
+int h3s_attention_batch(void* ctx, const void* q, const void* k, const void* v, int dt, int64_t B, int64_t S, int64_t H,
+                        int64_t D, int64_t stride, void* out, int out_dt);
+
+/* ---- additions without a counterpart in the reference ----------------------------------------------------------- */
+
+/* The Sage pre-pass alone (kernels/h3sycl.cpp:1733-1761 as a callable step, for parity checks and for callers that
+ * keep int8 q/k): iq, ik int8 [H, S, D]; sc float [2*H*nb + H*D] = q scales [H, nb], k scales [H, nb], k's channel
+ * mean [H*D], nb = ceil(S / 64). Queued on the context's stream. */
+int h3s_sage_prepass(void* ctx, const void* q, const void* k, int dt, int64_t S, int64_t H, int64_t D, int64_t stride,
+                     int8_t* iq, int8_t* ik, float* sc);
+/* The CUDA stream a context queues on (a cudaStream_t), for callers that order their own work with it. */
+void* h3s_stream(void* ctx);
+/* Self-test of the kernels' bounded waits: queues a kernel that waits `wait_ns` nanoseconds for an mbarrier nothing
+ * arrives at, gives up, and records the failure like any kernel of this library; the following h3s_wait returns -1.
+ * It faults nothing and leaves the context usable. */
+int h3s_selftest_wait_timeout(void* ctx, uint64_t wait_ns);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

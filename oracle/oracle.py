@@ -1,0 +1,197 @@
+"""ctypes front of the CPU oracle (liborc.so, built from oracle/sage_ref.cpp by oracle/Makefile).
+
+TEST INFRASTRUCTURE ONLY: the checker that tests/, ``__graft_entry__.smoke()`` and bench.py's CPU-baseline leg use.
+Nothing in the product imports this module.
+
+Every function takes and returns numpy arrays; an input may also be ``(array, element_offset)`` to point inside a wider
+buffer (q, k, v inside one qkv buffer of row stride 3*H*D). Element-type codes follow ``kernels/h3sycl.h:21`` of the reference
+(0 = float32, 1 = float16, 2 = bfloat16); float16/bfloat16 arrays are passed as their uint16 bit patterns.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liborc.so")
+F32, F16, BF16 = 0, 1, 2
+BLOCK = 64  # quantisation block (kernels/h3sycl.cpp:1681)
+
+_lib = None
+
+
+def build() -> str:
+    """Compiles liborc.so with oracle/Makefile (a no-op when it is current)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = ctypes.CDLL(LIB_PATH)
+        P, I64, I = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+        for name in ("orc_f32_to_f16", "orc_f16_to_f32", "orc_f32_to_bf16", "orc_bf16_to_f32"):
+            getattr(L, name).argtypes = [P, P, I64]
+            getattr(L, name).restype = None
+        L.orc_threads.restype = I
+        L.orc_set_threads.argtypes = [I]
+        L.orc_kmean.argtypes = [P, I, I64, I64, I64, I64, P]
+        L.orc_quant.argtypes = [P, I, I64, I64, I64, I64, P, P, P]
+        L.orc_sage_prepass.argtypes = [P, P, P, I, I64, I64, I64, I64, P, P, P, P]
+        L.orc_sage_rows.argtypes = [P, P, P, P, P, I64, I64, I64, ctypes.c_float, P, P, I64, P]
+        L.orc_sdpa_rows.argtypes = [P, P, P, I, I64, I64, I64, I64, P, P, I64, P]
+        L.orc_exact_rows.argtypes = [P, P, P, I, I64, I64, I64, I64, P, P, I64, P]
+        L.orc_attention.argtypes = [P, P, P, I, I64, I64, I64, I64, P, I, I64]
+        L.orc_attention.restype = I
+        _lib = L
+    return _lib
+
+
+def _p(a):
+    """Address of an array, or of element `off` of it when given as (array, off)."""
+    if a is None:
+        return None
+    off = 0
+    if isinstance(a, tuple):
+        a, off = a
+    assert a.flags["C_CONTIGUOUS"], "oracle arrays must be C-contiguous"
+    return a.ctypes.data + int(off) * a.itemsize
+
+
+def threads() -> int:
+    return lib().orc_threads()
+
+
+def set_threads(n: int) -> None:
+    lib().orc_set_threads(int(n))
+
+
+# ---- dtype helpers ---------------------------------------------------------------------------------------------------
+def f32_to_f16(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(x.shape, np.uint16)
+    lib().orc_f32_to_f16(_p(x), _p(y), x.size)
+    return y
+
+
+def f16_to_f32(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    y = np.empty(x.shape, np.float32)
+    lib().orc_f16_to_f32(_p(x), _p(y), x.size)
+    return y
+
+
+def f32_to_bf16(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(x.shape, np.uint16)
+    lib().orc_f32_to_bf16(_p(x), _p(y), x.size)
+    return y
+
+
+def bf16_to_f32(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.uint16)
+    y = np.empty(x.shape, np.float32)
+    lib().orc_bf16_to_f32(_p(x), _p(y), x.size)
+    return y
+
+
+def _dt_of(x: np.ndarray) -> int:
+    if x.dtype == np.float32:
+        return F32
+    raise TypeError("pass float16/bfloat16 data as uint16 bits together with an explicit dt")
+
+
+# ---- the Sage pre-pass -------------------------------------------------------------------------------------------------
+def kmean(k: np.ndarray, dt: int, S: int, H: int, D: int, stride: int) -> np.ndarray:
+    out = np.empty(H * D, np.float32)
+    lib().orc_kmean(_p(k), dt, S, H, D, stride, _p(out))
+    return out
+
+
+def quant(x: np.ndarray, dt: int, S: int, H: int, D: int, stride: int, mean: np.ndarray | None = None):
+    nb = (S + BLOCK - 1) // BLOCK
+    dst = np.empty((H, S, D), np.int8)
+    sc = np.empty((H, nb), np.float32)
+    lib().orc_quant(_p(x), dt, S, H, D, stride, _p(mean), _p(dst), _p(sc))
+    return dst, sc
+
+
+def sage_prepass(q, k, v, dt: int, S: int, H: int, D: int, stride: int):
+    """Returns (iq int8 [H,S,D], ik int8 [H,S,D], qs [H,nb], ks [H,nb], kmean [H*D], hv uint16 [H,S,D])."""
+    nb = (S + BLOCK - 1) // BLOCK
+    iq = np.empty((H, S, D), np.int8)
+    ik = np.empty((H, S, D), np.int8)
+    sc = np.empty(2 * H * nb + H * D, np.float32)
+    hv = np.empty((H, S, D), np.uint16)
+    lib().orc_sage_prepass(_p(q), _p(k), _p(v), dt, S, H, D, stride, _p(iq), _p(ik), _p(sc), _p(hv))
+    return iq, ik, sc[: H * nb].reshape(H, nb).copy(), sc[H * nb: 2 * H * nb].reshape(H, nb).copy(), \
+        sc[2 * H * nb:].copy(), hv
+
+
+def _rows(rows_h, rows_s):
+    rh = np.ascontiguousarray(rows_h, dtype=np.int64)
+    rs = np.ascontiguousarray(rows_s, dtype=np.int64)
+    assert rh.shape == rs.shape
+    return rh, rs
+
+
+def sage_rows(iq, ik, hv, qs, ks, S, H, D, rows_h, rows_s, scale: float | None = None) -> np.ndarray:
+    """Sage-semantics output rows (half bits [n, D]) for (head, token) pairs."""
+    rh, rs = _rows(rows_h, rows_s)
+    out = np.empty((rh.size, D), np.uint16)
+    sc = float(np.float32(1.0) / np.sqrt(np.float32(D))) if scale is None else scale
+    lib().orc_sage_rows(_p(iq), _p(ik), _p(hv), _p(np.ascontiguousarray(qs, np.float32)),
+                        _p(np.ascontiguousarray(ks, np.float32)), S, H, D, sc, _p(rh), _p(rs), rh.size, _p(out))
+    return out
+
+
+def sdpa_rows(q, k, v, dt, S, H, D, stride, rows_h, rows_s) -> np.ndarray:
+    """fp16 fused-SDPA-semantics output rows (half bits [n, D])."""
+    rh, rs = _rows(rows_h, rows_s)
+    out = np.empty((rh.size, D), np.uint16)
+    lib().orc_sdpa_rows(_p(q), _p(k), _p(v), dt, S, H, D, stride, _p(rh), _p(rs), rh.size, _p(out))
+    return out
+
+
+def exact_rows(q, k, v, dt, S, H, D, stride, rows_h, rows_s) -> np.ndarray:
+    """float64 softmax attention rows (float32 [n, D]): the tolerance anchor."""
+    rh, rs = _rows(rows_h, rows_s)
+    out = np.empty((rh.size, D), np.float32)
+    lib().orc_exact_rows(_p(q), _p(k), _p(v), dt, S, H, D, stride, _p(rh), _p(rs), rh.size, _p(out))
+    return out
+
+
+def attention(q, k, v, dt, S, H, D, stride, out_dt=F16, sage_min_s=8192) -> np.ndarray:
+    """h3s_attention semantics: out [S, H*D] in out_dt (uint16 bits for half/bf16, float32 for F32)."""
+    out = np.empty((S, H * D), np.float32 if out_dt == F32 else np.uint16)
+    rc = lib().orc_attention(_p(q), _p(k), _p(v), dt, S, H, D, stride, _p(out), out_dt, sage_min_s)
+    if rc != 0:
+        raise ValueError("orc_attention: the row stride is shorter than a row")
+    return out
+
+
+# ---- comparison, as the reference defines it (engine/h3-core/src/reference.rs:85-95) --------------------------------
+def compare(a: np.ndarray, b: np.ndarray) -> tuple[float, float]:
+    """(relative error |a-b|/|b|, cosine) over the whole arrays, in float64."""
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    d2 = float(np.sum((a - b) ** 2))
+    a2 = float(np.sum(a * a))
+    b2 = float(np.sum(b * b))
+    ab = float(np.sum(a * b))
+    return (d2 / max(b2, 1e-300)) ** 0.5, ab / max((a2 ** 0.5) * (b2 ** 0.5), 1e-300)
+
+
+def row_cosines(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Cosine per row of two [n, D] arrays, in float64."""
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    num = np.sum(a * b, axis=1)
+    den = np.maximum(np.linalg.norm(a, axis=1) * np.linalg.norm(b, axis=1), 1e-300)
+    return num / den

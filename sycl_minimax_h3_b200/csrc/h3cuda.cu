@@ -1,0 +1,679 @@
+// h3cuda.cu - libh3cuda.so: the attention subset of the reference's libh3sycl C ABI (kernels/h3sycl.h of
+// maxfridbe/sycl_minimax_h3) on NVIDIA B200, sm_100a.
+//
+//   context + memory    kernels/h3sycl.cpp:77-174, 241-402: a CUDA stream per context (the in-order queue), counted
+//                       allocations under a cap, grow-only scratch, pinned uploads on a second stream, per-thread errors
+//   dispatcher          kernels/h3sycl.cpp:1779-1816: Sage when S >= sage_min_s and libh3sage.so loads, else fp16 SDPA
+//   Sage pre-pass       kernels/h3sycl.cpp:1704-1764: K channel mean || Q quantiser, then K quantiser (prepass.cuh)
+//   plugin loader       kernels/h3sycl.cpp:1683-1701: dlopen libh3sage.so from this library's directory
+//   fp16 SDPA           kernels/h3sycl.cpp:1464-1674 (oneDNN's fused graph): attn_fwd<false> (attn.cuh), reading q, k,
+//                       v in place through TMA and writing the token-major output directly (no relayout copies)
+//
+// There is no CPU path and no score-table ("split") form: every attention call runs the tcgen05 kernels, or fails.
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+#include "../../include/h3cuda.h"
+#include "../../include/h3sage.h"
+#include "attn.cuh"
+#include "prepass.cuh"
+
+namespace {
+
+using namespace h3;
+
+thread_local std::string g_err;
+constexpr int kSageBlock = 64;   // kernels/h3sycl.cpp:1681
+
+struct DeviceGuard {            // makes `dev` current for the call and restores the caller's device after
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int now = -1;
+        if (prev >= 0 && cudaGetDevice(&now) == cudaSuccess && now != prev) cudaSetDevice(prev);
+    }
+};
+
+struct Ctx {
+    int device = 0;
+    cudaStream_t st = nullptr;
+    bool own_stream = false;
+    cudaStream_t aux = nullptr;                  // the K mean beside the Q quantiser
+    cudaEvent_t ev_fork = nullptr, ev_join = nullptr;
+    cudaStream_t cs = nullptr;                   // uploads (h3s_upload), made on first use
+    std::mutex cs_mu;
+    std::string name;
+    int* err = nullptr;                          // device error word of this context's kernels
+    bool profile = false, poison = false;
+    bool sage_want = true;
+    int64_t sage_min_s = 8192;
+    uint64_t wait_ns = 2000000000ull;
+    int sage_state = 0;                          // 0 not loaded yet, 1 ready, -1 unavailable
+    decltype(&h3sage_attention) sage_fn = nullptr;
+    decltype(&h3sage_attention_strided) sage_strided = nullptr;
+    decltype(&h3sage_error) sage_err = nullptr;
+    // scratch, grow-only
+    int8_t* sq = nullptr; size_t sq_cap = 0;     // q, k as int8 [H, S, D]
+    int8_t* sk = nullptr; size_t sk_cap = 0;
+    float* ss = nullptr; size_t ss_cap = 0;      // q scales, k scales, k mean
+    __half* hq = nullptr; size_t hq_cap = 0;     // half copies when the inputs cannot be read in place
+    __half* hk = nullptr; size_t hk_cap = 0;
+    __half* hv = nullptr; size_t hv_cap = 0;
+    __half* ao = nullptr; size_t ao_cap = 0;     // [H, S, D] output of a plugin without the strided entry
+    std::mutex mem_mu;
+    std::unordered_map<void*, size_t> mem;
+    size_t mem_used = 0, mem_cap = 0;
+
+    // A scratch buffer of at least n elements (+1/8 slack), counted against the cap; NULL with the reason in g_err.
+    template <typename T> T* grow(T*& p, size_t& cap, size_t n) {
+        if (n <= cap) return p;
+        const size_t want = n + (n >> 3);
+        std::lock_guard<std::mutex> l(mem_mu);
+        if (mem_used - cap * sizeof(T) + want * sizeof(T) > mem_cap) {
+            g_err = "a scratch buffer of " + std::to_string((want * sizeof(T)) >> 20) + " MiB would pass the device memory cap (" +
+                    std::to_string(mem_used >> 20) + " of " + std::to_string(mem_cap >> 20) + " MiB in use)";
+            return nullptr;
+        }
+        if (p) { cudaStreamSynchronize(st); cudaFree(p); }
+        mem_used -= cap * sizeof(T);
+        p = nullptr;
+        if (cudaMalloc(&p, want * sizeof(T)) != cudaSuccess) { p = nullptr; cudaGetLastError(); }
+        cap = p ? want : 0;
+        mem_used += cap * sizeof(T);
+        if (p && poison) cudaMemsetAsync(p, 0xff, want * sizeof(T), st);
+        if (!p) g_err = "the device refused a scratch buffer of " + std::to_string((want * sizeof(T)) >> 20) + " MiB";
+        return p;
+    }
+};
+
+int cuda_fail(const char* what, cudaError_t e) {
+    g_err = std::string(what) + ": " + cudaGetErrorString(e);
+    return -1;
+}
+
+// what every way of making a context shares (kernels/h3sycl.cpp:216-235)
+bool init(Ctx& c) {
+    cudaDeviceProp p{};
+    if (cudaGetDeviceProperties(&p, c.device) != cudaSuccess) { g_err = "cudaGetDeviceProperties failed"; return false; }
+    c.name = p.name;
+    double frac = 0.94;
+    if (const char* e = std::getenv("H3S_MEM_FRACTION")) frac = std::min(0.97, std::max(0.05, std::atof(e)));
+    c.mem_cap = (size_t) ((double) p.totalGlobalMem * frac);
+    c.profile = std::getenv("H3S_PROFILE") != nullptr;
+    c.poison = std::getenv("H3S_POISON") != nullptr;
+    if (const char* e = std::getenv("H3S_ATTN")) c.sage_want = std::strcmp(e, "onednn") != 0 && std::strcmp(e, "sdpa") != 0;
+    if (const char* e = std::getenv("H3S_SAGE_MIN_S")) c.sage_min_s = std::max<int64_t>(0, std::atoll(e));
+    if (const char* e = std::getenv("H3S_WAIT_MS")) c.wait_ns = (uint64_t) std::max(1, std::atoi(e)) * 1000000ull;
+    cudaError_t e;
+    if ((e = cudaStreamCreateWithFlags(&c.aux, cudaStreamNonBlocking)) != cudaSuccess ||
+        (e = cudaEventCreateWithFlags(&c.ev_fork, cudaEventDisableTiming)) != cudaSuccess ||
+        (e = cudaEventCreateWithFlags(&c.ev_join, cudaEventDisableTiming)) != cudaSuccess ||
+        (e = cudaMalloc(&c.err, sizeof(int))) != cudaSuccess || (e = cudaMemset(c.err, 0, sizeof(int))) != cudaSuccess) {
+        cuda_fail("context", e);
+        return false;
+    }
+    return true;
+}
+
+Ctx* make_ctx(int device, cudaStream_t st, bool own) {
+    DeviceGuard g(device);
+    auto* c = new Ctx;
+    c->device = device;
+    if (own) {
+        cudaError_t e = cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking);
+        if (e != cudaSuccess) { cuda_fail("cudaStreamCreate", e); delete c; return nullptr; }
+        c->own_stream = true;
+    } else {
+        c->st = st;
+    }
+    if (!init(*c)) {
+        if (c->own_stream) cudaStreamDestroy(c->st);
+        delete c;
+        return nullptr;
+    }
+    return c;
+}
+
+// ---- the Sage plugin (kernels/h3sycl.cpp:1683-1701) ----------------------------------------------------------------
+std::mutex g_sage_mu;
+bool sage_load(Ctx& c) {
+    if (c.sage_state) return c.sage_state > 0;
+    std::lock_guard<std::mutex> l(g_sage_mu);
+    c.sage_state = -1;
+    std::string path = "libh3sage.so";
+    Dl_info me;
+    if (dladdr((void*) &sage_load, &me) && me.dli_fname) {   // beside this library
+        std::string self = me.dli_fname;
+        const size_t slash = self.rfind('/');
+        if (slash != std::string::npos) path = self.substr(0, slash + 1) + path;
+    }
+    void* h = dlopen(path.c_str(), RTLD_NOW | RTLD_LOCAL);
+    if (!h) { std::fprintf(stderr, "h3cuda: no SageAttention (%s); attention on the fp16 SDPA kernel\n", dlerror()); return false; }
+    c.sage_fn = (decltype(c.sage_fn)) dlsym(h, "h3sage_attention");
+    c.sage_err = (decltype(c.sage_err)) dlsym(h, "h3sage_error");
+    c.sage_strided = (decltype(c.sage_strided)) dlsym(h, "h3sage_attention_strided");
+    if (!c.sage_fn || !c.sage_err) {
+        std::fprintf(stderr, "h3cuda: %s lacks h3sage_attention; attention stays on the fp16 SDPA kernel\n", path.c_str());
+        return false;
+    }
+    c.sage_state = 1;
+    return true;
+}
+
+// ---- phase timing (H3S_PROFILE) ------------------------------------------------------------------------------------
+struct Phases {
+    Ctx& c;
+    cudaEvent_t ev[4] = {};
+    int n = 0;
+    explicit Phases(Ctx& cc) : c(cc) {
+        if (!c.profile) return;
+        for (auto& e : ev) cudaEventCreate(&e);
+    }
+    void mark() {
+        if (c.profile && n < 4) cudaEventRecord(ev[n++], c.st);
+    }
+    void report(const char* what, int64_t S) {
+        if (!c.profile || n < 2) return;
+        cudaEventSynchronize(ev[n - 1]);
+        float ms[3] = {0, 0, 0};
+        for (int i = 1; i < n; ++i) cudaEventElapsedTime(&ms[i - 1], ev[i - 1], ev[i]);
+        std::fprintf(stderr, "h3cuda: attention (%s) S=%lld: pre-pass %.3f ms, attention %.3f, out %.3f\n", what,
+                     (long long) S, ms[0], ms[1], ms[2]);
+    }
+    ~Phases() {
+        if (!c.profile) return;
+        for (auto& e : ev) cudaEventDestroy(e);
+    }
+};
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+int esize(int dt) { return dt == F32 ? 4 : 2; }
+
+// ---- the Sage pre-pass (kernels/h3sycl.cpp:1733-1761) --------------------------------------------------------------
+template <int DT>
+int prepass_dt(Ctx& c, const void* q, const void* k, int64_t S, int64_t H, int64_t D, int64_t stride, int8_t* iq, int8_t* ik,
+               float* sc) {
+    const int64_t nb = (S + kSageBlock - 1) / kSageBlock;
+    float* qs = sc;
+    float* ks = sc + H * nb;
+    float* kmean = sc + 2 * H * nb;
+    const int C = (int) (H * D);
+    const int es = DtInfo<DT>::ES;
+    cudaError_t e;
+    // fork: the K mean runs on the aux stream beside the Q quantiser
+    if ((e = cudaEventRecord(c.ev_fork, c.st)) != cudaSuccess) return cuda_fail("event", e);
+    if ((e = cudaStreamWaitEvent(c.aux, c.ev_fork, 0)) != cudaSuccess) return cuda_fail("event", e);
+    CUtensorMap map;
+    bool tma = false;
+    if (aligned16(k) && (stride * es) % 16 == 0) {
+        auto enc = tensor_map_encoder();
+        if (enc) {
+            const cuuint64_t dims[2] = {(cuuint64_t) C, (cuuint64_t) S};
+            const cuuint64_t strides[1] = {(cuuint64_t) (stride * es)};
+            const cuuint32_t box[2] = {(cuuint32_t) kMeanCh, (cuuint32_t) kMeanRows};
+            const cuuint32_t estr[2] = {1, 1};
+            const CUtensorMapDataType ty = DT == F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                         : DT == BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+            tma = enc(&map, ty, 2, const_cast<void*>(k), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+                  CUDA_SUCCESS;
+        }
+    }
+    if (tma) {
+        using M = MeanCfg<DT>;
+        if ((e = cudaFuncSetAttribute(kmean_tma<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, M::SMEM)) != cudaSuccess)
+            return cuda_fail("kmean", e);
+        kmean_tma<DT><<<(C + kMeanCh - 1) / kMeanCh, kMeanThreads, M::SMEM, c.aux>>>(map, (int) S, C, kmean, c.err, c.wait_ns);
+    } else {
+        kmean_plain<DT><<<(C + 127) / 128, 128, 0, c.aux>>>(k, (int) S, C, (long long) stride, kmean);
+    }
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("kmean launch", e);
+    if ((e = cudaEventRecord(c.ev_join, c.aux)) != cudaSuccess) return cuda_fail("event", e);
+    const dim3 grid((unsigned) nb, (unsigned) H);
+    const bool vq = aligned16(q) && (stride * es) % 16 == 0 && (D * es) % 16 == 0;
+    const bool vk = aligned16(k) && (stride * es) % 16 == 0 && (D * es) % 16 == 0;
+    if (vq) quant_rows<DT, 128, true><<<grid, kQuantThreads, 0, c.st>>>(q, (int) S, stride, nullptr, iq, qs, (int) nb);
+    else quant_rows<DT, 128, false><<<grid, kQuantThreads, 0, c.st>>>(q, (int) S, stride, nullptr, iq, qs, (int) nb);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("quantise q", e);
+    if ((e = cudaStreamWaitEvent(c.st, c.ev_join, 0)) != cudaSuccess) return cuda_fail("event", e);
+    if (vk) quant_rows<DT, 128, true><<<grid, kQuantThreads, 0, c.st>>>(k, (int) S, stride, kmean, ik, ks, (int) nb);
+    else quant_rows<DT, 128, false><<<grid, kQuantThreads, 0, c.st>>>(k, (int) S, stride, kmean, ik, ks, (int) nb);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("quantise k", e);
+    return 0;
+}
+
+int prepass(Ctx& c, const void* q, const void* k, int dt, int64_t S, int64_t H, int64_t D, int64_t stride, int8_t* iq,
+            int8_t* ik, float* sc) {
+    if (D != 128) { g_err = "the Sage pre-pass takes D = 128 (got " + std::to_string(D) + ")"; return -1; }
+    switch (dt) {
+        case F16: return prepass_dt<F16>(c, q, k, S, H, D, stride, iq, ik, sc);
+        case BF16: return prepass_dt<BF16>(c, q, k, S, H, D, stride, iq, ik, sc);
+        case F32: return prepass_dt<F32>(c, q, k, S, H, D, stride, iq, ik, sc);
+        default: g_err = "unknown element type " + std::to_string(dt); return -1;
+    }
+}
+
+// any dt token rows -> half [H, S, D] for one sequence
+int to_half(Ctx& c, const void* src, int dt, int64_t S, int64_t H, int64_t D, int64_t stride, __half* dst) {
+    const int blocks = 148 * 8;
+    switch (dt) {
+        case F16: to_half_hsd<F16><<<blocks, 256, 0, c.st>>>(src, (int) S, (int) H, (int) D, stride, dst); break;
+        case BF16: to_half_hsd<BF16><<<blocks, 256, 0, c.st>>>(src, (int) S, (int) H, (int) D, stride, dst); break;
+        default: to_half_hsd<F32><<<blocks, 256, 0, c.st>>>(src, (int) S, (int) H, (int) D, stride, dst); break;
+    }
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail("to half", e);
+}
+
+// half [H, S, D] -> out_dt [S, H*D] (kernels/h3sycl.cpp:1769-1771), for a plugin without the strided entry point
+__global__ void hsd_to_rows(const __half* src, int S, int H, int D, void* out, int out_dt) {
+    const size_t n = (size_t) S * H * D;
+    for (size_t i = blockIdx.x * (size_t) blockDim.x + threadIdx.x; i < n; i += (size_t) gridDim.x * blockDim.x) {
+        const size_t d = i % D, hh = (i / D) % H, s = i / ((size_t) D * H);
+        const float v = __half2float(src[(hh * S + s) * D + d]);
+        if (out_dt == F16) reinterpret_cast<__half*>(out)[i] = __float2half_rn(v);
+        else if (out_dt == BF16) reinterpret_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+        else reinterpret_cast<float*>(out)[i] = v;
+    }
+}
+
+// ---- Form 0: SageAttention v1 (kernels/h3sycl.cpp:1704-1777). 1 = not a shape this path takes. ----------------------
+int attention_sage(Ctx& c, const void* q, const void* k, const void* v, int dt, int64_t S, int64_t H, int64_t D,
+                   int64_t stride, void* out, int out_dt) {
+    if (D != 128 || S > INT32_MAX / D / H) return 1;
+    const size_t n = (size_t) S * H * D;
+    const int64_t nb = (S + kSageBlock - 1) / kSageBlock;
+    int8_t* iq = c.grow(c.sq, c.sq_cap, n);
+    int8_t* ik = c.grow(c.sk, c.sk_cap, n);
+    float* sc = c.grow(c.ss, c.ss_cap, (size_t) (2 * H * nb + H * D));
+    if (!iq || !ik || !sc) return -1;
+    Phases ph(c);
+    ph.mark();
+    if (prepass(c, q, k, dt, S, H, D, stride, iq, ik, sc) != 0) return -1;
+    // v in place when the kernel can read it (half, 16-byte aligned rows); else a half copy by head
+    const void* vp = v;
+    int64_t v_tok = stride, v_head = D;
+    const bool v_inplace = dt == F16 && aligned16(v) && (stride * 2) % 16 == 0 && c.sage_strided;
+    if (!v_inplace) {
+        __half* hv = c.grow(c.hv, c.hv_cap, n);
+        if (!hv || to_half(c, v, dt, S, H, D, stride, hv) != 0) return -1;
+        vp = hv;
+        v_tok = D;
+        v_head = S * D;
+    }
+    ph.mark();
+    cudaStream_t st = c.st;
+    const float scale = 1.0f / std::sqrt((float) D);
+    const float* qs = sc;
+    const float* ks = sc + H * nb;
+    if (c.sage_strided) {
+        if (c.sage_strided(&st, iq, ik, vp, v_tok, v_head, out, out_dt, H * D, D, qs, ks, kSageBlock, S, H, D, scale, c.err,
+                           c.wait_ns) != 0) {
+            g_err = c.sage_err();
+            return -2;
+        }
+        ph.mark();
+    } else {
+        __half* ao = c.grow(c.ao, c.ao_cap, n);
+        if (!ao) return -1;
+        if (c.sage_fn(&st, iq, ik, vp, ao, qs, ks, kSageBlock, S, H, D, scale) != 0) { g_err = c.sage_err(); return -2; }
+        ph.mark();
+        hsd_to_rows<<<148 * 8, 256, 0, c.st>>>(ao, (int) S, (int) H, (int) D, out, out_dt);
+        const cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return cuda_fail("out relayout", e);
+    }
+    ph.mark();
+    ph.report("sage", S);
+    return 0;
+}
+
+// ---- Form 1: fp16 SDPA over B sequences (kernels/h3sycl.cpp:1464-1674) ------------------------------------------------
+int attention_sdpa(Ctx& c, const void* q, const void* k, const void* v, int dt, int64_t B, int64_t S, int64_t H, int64_t D,
+                   int64_t stride, void* out, int out_dt) {
+    if (D != 128) { g_err = "attention: head size " + std::to_string(D) + " (128 only on this build)"; return -1; }
+    if (S > INT32_MAX / 2 || B * H > 65535) { g_err = "attention: sequence or head count out of range"; return -1; }
+    Phases ph(c);
+    ph.mark();
+    const bool inplace = dt == F16 && aligned16(q) && aligned16(k) && aligned16(v) && (stride * 2) % 16 == 0;
+    const void *qp = q, *kp = k, *vp = v;
+    int order = 1;
+    int64_t tok = stride * 2, head = D * 2, seq = S * stride * 2;
+    if (!inplace) {
+        const size_t n = (size_t) B * S * H * D;
+        __half* hq = c.grow(c.hq, c.hq_cap, n);
+        __half* hk = c.grow(c.hk, c.hk_cap, n);
+        __half* hv = c.grow(c.hv, c.hv_cap, n);
+        if (!hq || !hk || !hv) return -1;
+        const size_t ei = (size_t) esize(dt), per = (size_t) S * H * D;
+        for (int64_t b = 0; b < B; ++b) {
+            const size_t io = (size_t) (b * S * stride) * ei;
+            if (to_half(c, (const char*) q + io, dt, S, H, D, stride, hq + b * per) ||
+                to_half(c, (const char*) k + io, dt, S, H, D, stride, hk + b * per) ||
+                to_half(c, (const char*) v + io, dt, S, H, D, stride, hv + b * per))
+                return -1;
+        }
+        qp = hq; kp = hk; vp = hv;
+        order = 0;
+        tok = D * 2; head = S * D * 2; seq = H * S * D * 2;
+    }
+    ph.mark();
+    CUtensorMap mq, mk, mv;
+    std::string e = make_rows_map(&mq, qp, false, D, S, H, B, tok, head, seq, order);
+    if (e.empty()) e = make_rows_map(&mk, kp, false, D, S, H, B, tok, head, seq, order);
+    if (e.empty()) e = make_rows_map(&mv, vp, false, D, S, H, B, tok, head, seq, order);
+    if (!e.empty()) { g_err = "attention: " + e; return -1; }
+    AttnArgs a{};
+    a.S = (int) S;
+    a.H = (int) H;
+    a.n_kv = (int) ((S + kTileN - 1) / kTileN);
+    a.scale_log2 = (1.0f / std::sqrt((float) D)) * 1.4426950408889634f;
+    a.out = out;
+    a.out_seq = S * H * D;
+    a.out_tok = H * D;
+    a.out_head = D;
+    a.out_dt = out_dt;
+    a.out_vec = aligned16(out) ? 1 : 0;
+    a.q_order = a.k_order = a.v_order = order;
+    a.err = c.err;
+    a.wait_ns = c.wait_ns;
+    const cudaError_t ce = launch_attn<false>(mq, mk, mv, a, (int) B, c.st);
+    if (ce != cudaSuccess) return cuda_fail("attention launch", ce);
+    ph.mark();
+    ph.mark();
+    ph.report("sdpa", S);
+    return 0;
+}
+
+int check_dt(int dt) { return dt == F32 || dt == F16 || dt == BF16; }
+
+// the wait self-test: an mbarrier nothing arrives at
+__global__ void wait_timeout_kernel(int* err, unsigned long long wait_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && !mbar_wait(&bar, 0, wait_ns, nullptr)) atomicOr(err, 16);
+    __syncthreads();
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* h3s_last_error(void) { return g_err.c_str(); }
+
+void* h3s_open(void) { return h3s_open_gpu(0); }
+
+int h3s_gpu_count(void) {
+    int n = 0;
+    const cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) return cuda_fail("cudaGetDeviceCount", e);
+    return n;
+}
+
+int h3s_gpu_info(int index, char* name, int name_len, uint64_t* mem_bytes, char* pci, int pci_len) {
+    const int n = h3s_gpu_count();
+    if (n < 0) return -1;
+    if (index < 0 || index >= n) { g_err = "no GPU " + std::to_string(index); return -1; }
+    cudaDeviceProp p{};
+    const cudaError_t e = cudaGetDeviceProperties(&p, index);
+    if (e != cudaSuccess) return cuda_fail("cudaGetDeviceProperties", e);
+    if (name && name_len > 0) std::snprintf(name, (size_t) name_len, "%s", p.name);
+    if (mem_bytes) *mem_bytes = p.totalGlobalMem;
+    if (pci && pci_len > 0) std::snprintf(pci, (size_t) pci_len, "%04x:%02x:%02x.0", p.pciDomainID, p.pciBusID, p.pciDeviceID);
+    return 0;
+}
+
+void* h3s_open_gpu(int index) {
+    const int n = h3s_gpu_count();
+    if (n < 0) return nullptr;
+    if (index < 0 || index >= n) {
+        g_err = "no GPU " + std::to_string(index) + " (" + std::to_string(n) + " found)";
+        return nullptr;
+    }
+    return make_ctx(index, nullptr, true);
+}
+
+void* h3s_create(void* stream) {
+    int dev = 0;
+    const cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) { cuda_fail("cudaGetDevice", e); return nullptr; }
+    return make_ctx(dev, stream ? *static_cast<cudaStream_t*>(stream) : nullptr, false);
+}
+
+void h3s_destroy(void* ctx) {
+    auto* c = static_cast<Ctx*>(ctx);
+    if (!c) return;
+    DeviceGuard g(c->device);
+    cudaStreamSynchronize(c->st);
+    cudaStreamSynchronize(c->aux);
+    if (c->cs) { cudaStreamSynchronize(c->cs); cudaStreamDestroy(c->cs); }
+    for (void* p : {(void*) c->sq, (void*) c->sk, (void*) c->ss, (void*) c->hq, (void*) c->hk, (void*) c->hv, (void*) c->ao,
+                    (void*) c->err})
+        if (p) cudaFree(p);
+    for (auto& kv : c->mem) cudaFree(kv.first);
+    cudaEventDestroy(c->ev_fork);
+    cudaEventDestroy(c->ev_join);
+    cudaStreamDestroy(c->aux);
+    if (c->own_stream) cudaStreamDestroy(c->st);
+    delete c;
+}
+
+const char* h3s_device_name(void* ctx) { return static_cast<Ctx*>(ctx)->name.c_str(); }
+uint64_t h3s_mem_cap(void* ctx) { return static_cast<Ctx*>(ctx)->mem_cap; }
+uint64_t h3s_mem_used(void* ctx) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    std::lock_guard<std::mutex> l(c.mem_mu);
+    return c.mem_used;
+}
+uint64_t h3s_mem_free(void* ctx) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    DeviceGuard g(c.device);
+    size_t f = 0, t = 0;
+    if (cudaMemGetInfo(&f, &t) != cudaSuccess) { cudaGetLastError(); return 0; }
+    return f;
+}
+
+void* h3s_alloc(void* ctx, uint64_t bytes) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    DeviceGuard g(c.device);
+    std::lock_guard<std::mutex> l(c.mem_mu);
+    if (c.mem_used + bytes > c.mem_cap) {
+        g_err = "h3s_alloc: " + std::to_string(bytes >> 20) + " MiB would pass the device memory cap (" +
+                std::to_string(c.mem_used >> 20) + " of " + std::to_string(c.mem_cap >> 20) + " MiB in use)";
+        return nullptr;
+    }
+    void* p = nullptr;
+    const cudaError_t e = cudaMalloc(&p, bytes ? bytes : 1);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        g_err = "h3s_alloc: the device refused " + std::to_string(bytes >> 20) + " MiB (" + cudaGetErrorString(e) + ")";
+        return nullptr;
+    }
+    if (c.poison) { cudaMemset(p, 0xff, bytes ? bytes : 1); }
+    c.mem.emplace(p, bytes);
+    c.mem_used += bytes;
+    return p;
+}
+
+void h3s_free(void* ctx, void* p) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    if (!p) return;
+    DeviceGuard g(c.device);
+    cudaStreamSynchronize(c.st);                 // nothing queued may still read or write it
+    if (c.cs) cudaStreamSynchronize(c.cs);       // nor an upload into it
+    std::lock_guard<std::mutex> l(c.mem_mu);
+    auto it = c.mem.find(p);
+    if (it == c.mem.end()) return;
+    c.mem_used -= it->second;
+    c.mem.erase(it);
+    cudaFree(p);
+}
+
+int h3s_write(void* ctx, void* dst, const void* src_host, uint64_t bytes) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    DeviceGuard g(c.device);
+    cudaError_t e = cudaMemcpyAsync(dst, src_host, bytes, cudaMemcpyHostToDevice, c.st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c.st);
+    return e == cudaSuccess ? 0 : cuda_fail("h3s_write", e);
+}
+
+int h3s_read(void* ctx, void* dst_host, const void* src, uint64_t bytes) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    DeviceGuard g(c.device);
+    cudaError_t e = cudaMemcpyAsync(dst_host, src, bytes, cudaMemcpyDeviceToHost, c.st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c.st);
+    return e == cudaSuccess ? 0 : cuda_fail("h3s_read", e);
+}
+
+int h3s_copy(void* ctx, void* dst, const void* src, uint64_t bytes) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    DeviceGuard g(c.device);
+    const cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, c.st);
+    return e == cudaSuccess ? 0 : cuda_fail("h3s_copy", e);
+}
+
+int h3s_wait(void* ctx) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    DeviceGuard g(c.device);
+    cudaError_t e = cudaStreamSynchronize(c.st);
+    if (e != cudaSuccess) return cuda_fail("h3s_wait", e);
+    int code = 0;
+    e = cudaMemcpy(&code, c.err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail("h3s_wait", e);
+    if (code) {
+        cudaMemset(c.err, 0, sizeof(int));
+        g_err = "h3s_wait: a wait inside a kernel gave up after " + std::to_string(c.wait_ns / 1000000) +
+                " ms (code " + std::to_string(code) + "); its results are not valid";
+        return -1;
+    }
+    return 0;
+}
+
+void* h3s_alloc_host(void* ctx, uint64_t bytes) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    DeviceGuard g(c.device);
+    void* p = nullptr;
+    const cudaError_t e = cudaMallocHost(&p, bytes ? bytes : 1);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        g_err = "h3s_alloc_host: the runtime refused " + std::to_string(bytes >> 20) + " MiB of pinned memory";
+        return nullptr;
+    }
+    return p;
+}
+
+void h3s_free_host(void* ctx, void* p) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    if (!p) return;
+    DeviceGuard g(c.device);
+    if (c.cs) cudaStreamSynchronize(c.cs);
+    cudaFreeHost(p);
+}
+
+int h3s_upload(void* ctx, void* dst, const void* src_pinned, uint64_t bytes) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    DeviceGuard g(c.device);
+    cudaPointerAttributes as{}, ad{};
+    if (cudaPointerGetAttributes(&as, src_pinned) != cudaSuccess || cudaPointerGetAttributes(&ad, dst) != cudaSuccess ||
+        as.type != cudaMemoryTypeHost || ad.type != cudaMemoryTypeDevice) {
+        cudaGetLastError();
+        g_err = "h3s_upload: the source must be h3s_alloc_host memory and the destination device memory";
+        return -1;
+    }
+    {
+        std::lock_guard<std::mutex> l(c.cs_mu);
+        if (!c.cs) {
+            const cudaError_t e = cudaStreamCreateWithFlags(&c.cs, cudaStreamNonBlocking);
+            if (e != cudaSuccess) return cuda_fail("h3s_upload", e);
+        }
+    }
+    const cudaError_t e = cudaMemcpyAsync(dst, src_pinned, bytes, cudaMemcpyHostToDevice, c.cs);
+    return e == cudaSuccess ? 0 : cuda_fail("h3s_upload", e);
+}
+
+int h3s_upload_wait(void* ctx) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    DeviceGuard g(c.device);
+    if (!c.cs) return 0;
+    const cudaError_t e = cudaStreamSynchronize(c.cs);
+    return e == cudaSuccess ? 0 : cuda_fail("h3s_upload_wait", e);
+}
+
+int h3s_attention(void* ctx, const void* q, const void* k, const void* v, int dt, int64_t S, int64_t H, int64_t D,
+                  int64_t stride, void* out, int out_dt) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    if (S <= 0 || H <= 0 || D <= 0) return 0;
+    if (stride < H * D) { g_err = "h3s_attention: the row stride is shorter than a row"; return -1; }
+    if (!check_dt(dt) || !check_dt(out_dt)) { g_err = "h3s_attention: unknown element type"; return -1; }
+    DeviceGuard g(c.device);
+    if (c.sage_want && S >= c.sage_min_s && sage_load(c)) {
+        const int rc = attention_sage(c, q, k, v, dt, S, H, D, stride, out, out_dt);
+        if (rc == 0) return 0;
+        if (rc == -1) return -1;
+        if (rc == -2) {   // the plugin refused: as the reference, log, wait, and stay on the SDPA kernel from now on
+            std::fprintf(stderr, "h3cuda: SageAttention failed (%s); attention stays on the fp16 SDPA kernel\n", g_err.c_str());
+            cudaStreamSynchronize(c.st);
+            c.sage_state = -1;
+        }
+    }
+    return attention_sdpa(c, q, k, v, dt, 1, S, H, D, stride, out, out_dt);
+}
+
+int h3s_attention_batch(void* ctx, const void* q, const void* k, const void* v, int dt, int64_t B, int64_t S, int64_t H,
+                        int64_t D, int64_t stride, void* out, int out_dt) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    if (B <= 0 || S <= 0 || H <= 0 || D <= 0) return 0;
+    if (stride < H * D) { g_err = "h3s_attention_batch: the row stride is shorter than a row"; return -1; }
+    if (!check_dt(dt) || !check_dt(out_dt)) { g_err = "h3s_attention_batch: unknown element type"; return -1; }
+    const bool sage = c.sage_want && S >= c.sage_min_s;
+    if (B > 1 && !sage) {
+        DeviceGuard g(c.device);
+        return attention_sdpa(c, q, k, v, dt, B, S, H, D, stride, out, out_dt);
+    }
+    const size_t ei = (size_t) esize(dt), eo = (size_t) esize(out_dt);
+    for (int64_t b = 0; b < B; ++b) {
+        const size_t io = (size_t) (b * S * stride) * ei, oo = (size_t) (b * S * H * D) * eo;
+        const int rc = h3s_attention(ctx, (const char*) q + io, (const char*) k + io, (const char*) v + io, dt, S, H, D, stride,
+                                     (char*) out + oo, out_dt);
+        if (rc != 0) return rc;
+    }
+    return 0;
+}
+
+int h3s_sage_prepass(void* ctx, const void* q, const void* k, int dt, int64_t S, int64_t H, int64_t D, int64_t stride,
+                     int8_t* iq, int8_t* ik, float* sc) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    if (S <= 0 || H <= 0 || D <= 0) return 0;
+    if (stride < H * D) { g_err = "h3s_sage_prepass: the row stride is shorter than a row"; return -1; }
+    if (!check_dt(dt)) { g_err = "h3s_sage_prepass: unknown element type"; return -1; }
+    DeviceGuard g(c.device);
+    return prepass(c, q, k, dt, S, H, D, stride, iq, ik, sc);
+}
+
+void* h3s_stream(void* ctx) { return (void*) static_cast<Ctx*>(ctx)->st; }
+
+int h3s_selftest_wait_timeout(void* ctx, uint64_t wait_ns) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    DeviceGuard g(c.device);
+    wait_timeout_kernel<<<1, 32, 0, c.st>>>(c.err, (unsigned long long) wait_ns);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : cuda_fail("h3s_selftest_wait_timeout", e);
+}
+
+}  // extern "C"

@@ -1,0 +1,215 @@
+// prepass.cuh - the Sage pre-pass for sm_100a (kernels/h3sycl.cpp:1704-1764 of the reference), bit-exact with it:
+//
+//   kmean     kmean[h*D+d] = (((0 + k_0) + k_1) + ... + k_{S-1}) / (float) S: one fp32 chain per channel in token order
+//             (the reference's loop, kernels/h3sycl.cpp:1733-1737). A chain cannot be split without changing its bits,
+//             so the work is shaped around it: a TMA ring streams 64-token x 64-channel tiles of k into shared memory
+//             (96 KB in flight per CTA) while 64 threads run the 64 chains over each tile.
+//   quant     per (head, 64-row block): m = max|x - mean|, inv = m > 0 ? 127/m : 0, scale = m/127,
+//             q = clamp(round(x * inv), -127, 127), round half away from zero (kernels/h3sycl.cpp:1738-1761).
+//             One CTA per block; the 64 x D values are read once with 16-byte loads and held in registers between the
+//             absmax and the quantisation.
+//   to_half   any dt -> half [H, S, D] (kernels/h3sycl.cpp:1762-1764), only where the attention cannot read in place.
+//
+// All arithmetic uses the round-to-nearest intrinsics (__fadd_rn, __fsub_rn, __fmul_rn, __fdiv_rn), which the compiler
+// never fuses into FMAs, so the results do not depend on contraction.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "attn.cuh"
+#include "ptx.cuh"
+
+namespace h3 {
+
+template <int DT> struct DtInfo;
+template <> struct DtInfo<F32> { static constexpr int ES = 4; };
+template <> struct DtInfo<F16> { static constexpr int ES = 2; };
+template <> struct DtInfo<BF16> { static constexpr int ES = 2; };
+
+template <int DT>
+__device__ __forceinline__ float ld1(const void* p, size_t i) {
+    if constexpr (DT == F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+    else if constexpr (DT == BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+    else return reinterpret_cast<const float*>(p)[i];
+}
+// 16 bytes -> 16/ES floats
+template <int DT>
+__device__ __forceinline__ void ld16(const void* p, float* out) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    if constexpr (DT == F32) {
+        out[0] = __uint_as_float(u.x); out[1] = __uint_as_float(u.y); out[2] = __uint_as_float(u.z); out[3] = __uint_as_float(u.w);
+    } else {
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint16_t lo = (uint16_t) (w[i] & 0xffffu), hi = (uint16_t) (w[i] >> 16);
+            if constexpr (DT == F16) {
+                out[2 * i] = __half2float(__ushort_as_half(lo));
+                out[2 * i + 1] = __half2float(__ushort_as_half(hi));
+            } else {
+                out[2 * i] = __uint_as_float((uint32_t) lo << 16);
+                out[2 * i + 1] = __uint_as_float((uint32_t) hi << 16);
+            }
+        }
+    }
+}
+
+// ---- K mean, TMA ring ----------------------------------------------------------------------------------------------
+constexpr int kMeanCh = 64;          // channels per CTA (one chain per thread)
+constexpr int kMeanRows = 64;        // tokens per tile
+constexpr int kMeanRingBytes = 96 * 1024;
+constexpr int kMeanThreads = 96;     // warp 0: producer; warps 1-2: the 64 chains
+
+template <int DT>
+struct MeanCfg {
+    static constexpr int TILE = kMeanCh * kMeanRows * DtInfo<DT>::ES;
+    static constexpr int NS = kMeanRingBytes / TILE;
+    static constexpr int SMEM = NS * TILE + 2 * NS * 8 + 16 + 128;
+};
+
+// map: 2-D over k, dims (H*D channels, S tokens), row stride in bytes, box (64, 64), no swizzle
+template <int DT>
+__global__ void __launch_bounds__(kMeanThreads) kmean_tma(const __grid_constant__ CUtensorMap map, int S, int C,
+                                                          float* kmean, int* err, unsigned long long wait_ns) {
+    using M = MeanCfg<DT>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + M::NS * M::TILE);
+    uint64_t* empty = full + M::NS;
+    volatile int* abort = reinterpret_cast<volatile int*>(empty + M::NS);
+    const int c0 = blockIdx.x * kMeanCh;
+    const int ntile = (S + kMeanRows - 1) / kMeanRows;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < M::NS; ++i) { mbar_init(full + i, 1); mbar_init(empty + i, kMeanCh); }
+        *abort = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        if (threadIdx.x == 0) {
+            tma_prefetch_desc(&map);
+            int last[M::NS];
+            for (int i = 0; i < M::NS; ++i) last[i] = -1;
+            bool ok = true;
+            for (int t = 0; t < ntile; ++t) {
+                const int st = t % M::NS;
+                if (t >= M::NS && !mbar_wait(empty + st, ((t / M::NS) - 1) & 1, wait_ns, abort)) { ok = false; break; }
+                mbar_expect_tx(full + st, M::TILE);
+                tma_load_2d(sm + st * M::TILE, &map, full + st, c0, t * kMeanRows);
+                last[st] = t;
+            }
+            if (!ok) { atomicOr(err, kErrPrepass); *abort = 1; }
+            for (int i = 0; i < M::NS; ++i)
+                if (last[i] >= 0) mbar_wait(full + i, (last[i] / M::NS) & 1, wait_ns, nullptr);
+        }
+        __syncwarp();
+    } else {
+        const int c = threadIdx.x - 32;
+        float sum = 0.0f;
+        bool ok = true;
+        for (int t = 0; t < ntile; ++t) {
+            const int st = t % M::NS;
+            if (!mbar_wait(full + st, (t / M::NS) & 1, wait_ns, abort)) { ok = false; break; }
+            const uint8_t* tile = sm + st * M::TILE;
+            const int rows = min(kMeanRows, S - t * kMeanRows);
+            if (rows == kMeanRows) {
+#pragma unroll 16
+                for (int r = 0; r < kMeanRows; ++r)
+                    sum = __fadd_rn(sum, ld1<DT>(tile, (size_t) (r * kMeanCh + c)));
+            } else {
+                for (int r = 0; r < rows; ++r) sum = __fadd_rn(sum, ld1<DT>(tile, (size_t) (r * kMeanCh + c)));
+            }
+            mbar_arrive(empty + st);
+        }
+        if (!ok) { atomicOr(err, kErrPrepass); *abort = 1; }
+        else if (c0 + c < C) kmean[c0 + c] = __fdiv_rn(sum, (float) S);
+    }
+    __syncthreads();
+}
+
+// Any alignment: one thread per channel reading k directly (the fallback for strides TMA cannot take).
+template <int DT>
+__global__ void kmean_plain(const void* k, int S, int C, long long stride, float* kmean) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= C) return;
+    float sum = 0.0f;
+    for (int t = 0; t < S; ++t) sum = __fadd_rn(sum, ld1<DT>(k, (size_t) t * (size_t) stride + (size_t) c));
+    kmean[c] = __fdiv_rn(sum, (float) S);
+}
+
+// ---- quantiser -----------------------------------------------------------------------------------------------------
+constexpr int kQuantThreads = 128;
+
+// grid (nb, H); src rows at element stride `stride`, head h at column h*D; dst int8 [H, S, D]; scales [H, nb].
+// VEC: 16-byte loads (every row start 16-byte aligned, checked on the host).
+template <int DT, int D, bool VEC>
+__global__ void __launch_bounds__(kQuantThreads) quant_rows(const void* src, int S, long long stride, const float* mean,
+                                                            int8_t* dst, float* scales, int nb) {
+    constexpr int EPC = 16 / DtInfo<DT>::ES;          // elements per 16-byte chunk
+    constexpr int CPR = D / EPC;                      // chunks per row
+    constexpr int NCH = 64 * CPR / kQuantThreads;     // chunks per thread
+    static_assert(kQuantThreads % CPR == 0, "a thread keeps one column chunk");
+    const int b = blockIdx.x, h = blockIdx.y;
+    const int r0 = b * 64, rows = min(64, S - r0);
+    const int col = (threadIdx.x % CPR) * EPC;        // this thread's first feature
+    const int rsub = threadIdx.x / CPR;               // first row; then every kQuantThreads/CPR rows
+    constexpr int RSTEP = kQuantThreads / CPR;
+    float mu[EPC];
+#pragma unroll
+    for (int e = 0; e < EPC; ++e) mu[e] = mean ? mean[h * D + col + e] : 0.0f;
+    float x[NCH][EPC];
+    float m = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NCH; ++i) {
+        const int r = rsub + i * RSTEP;
+        if (r < rows) {
+            const size_t base = (size_t) (r0 + r) * (size_t) stride + (size_t) (h * D + col);
+            if constexpr (VEC) {
+                ld16<DT>(reinterpret_cast<const uint8_t*>(src) + base * DtInfo<DT>::ES, x[i]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < EPC; ++e) x[i][e] = ld1<DT>(src, base + e);
+            }
+#pragma unroll
+            for (int e = 0; e < EPC; ++e) {
+                x[i][e] = __fsub_rn(x[i][e], mu[e]);
+                m = fmaxf(m, fabsf(x[i][e]));
+            }
+        }
+    }
+    // block absmax
+    __shared__ float red[kQuantThreads / 32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    __syncthreads();
+    m = red[0];
+#pragma unroll
+    for (int w = 1; w < kQuantThreads / 32; ++w) m = fmaxf(m, red[w]);
+    const float inv = m > 0.0f ? __fdiv_rn(127.0f, m) : 0.0f;
+    if (threadIdx.x == 0) scales[(size_t) h * nb + b] = __fdiv_rn(m, 127.0f);
+#pragma unroll
+    for (int i = 0; i < NCH; ++i) {
+        const int r = rsub + i * RSTEP;
+        if (r < rows) {
+            int8_t qv[EPC];
+#pragma unroll
+            for (int e = 0; e < EPC; ++e) qv[e] = (int8_t) fminf(127.0f, fmaxf(-127.0f, roundf(__fmul_rn(x[i][e], inv))));
+            int8_t* d = dst + ((size_t) h * S + r0 + r) * D + col;
+            if constexpr (EPC == 8) *reinterpret_cast<uint2*>(d) = *reinterpret_cast<const uint2*>(qv);
+            else *reinterpret_cast<uint32_t*>(d) = *reinterpret_cast<const uint32_t*>(qv);
+        }
+    }
+}
+
+// any dt, token rows -> half [H, S, D] (one sequence)
+template <int DT>
+__global__ void to_half_hsd(const void* src, int S, int H, int D, long long stride, __half* dst) {
+    const size_t n = (size_t) S * H * D;
+    for (size_t i = blockIdx.x * (size_t) blockDim.x + threadIdx.x; i < n; i += (size_t) gridDim.x * blockDim.x) {
+        const size_t d = i % D, t = (i / D) % S, hh = i / ((size_t) D * S);
+        dst[i] = __float2half_rn(ld1<DT>(src, t * (size_t) stride + hh * D + d));
+    }
+}
+
+}  // namespace h3

@@ -1,0 +1,91 @@
+"""The reference engine's attention operators over torch tensors, on libh3cuda.so.
+
+A Python restatement of ``engine/h3-core/src/ops.rs`` of maxfridbe/sycl_minimax_h3 for this path: ``Rows`` (ops.rs
+:299-324) describes token rows of ``heads x dim`` features inside a wider row-major buffer - how q, k and v sit inside
+the qkv linear's output (offset i*H*D, stride 3*H*D) - and ``attention`` / ``attention_batch`` (ops.rs:405-461) check
+the layouts exactly as the reference does, then call ``h3s_attention`` / ``h3s_attention_batch``.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from .native import Context, H3Error, dt_code
+
+_ctx: dict[tuple[int, int], Context] = {}
+
+
+def context(device=None) -> Context:
+    """The h3s context of a device around PyTorch's current stream on it (made once per (device, stream))."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else torch.device(device).index or 0)
+    with torch.cuda.device(dev):
+        s = torch.cuda.current_stream()
+        key = (dev.index, int(s.cuda_stream))
+        if key not in _ctx:
+            _ctx[key] = Context(s)
+        return _ctx[key]
+
+
+@dataclass(frozen=True)
+class Rows:
+    """Token rows of ``heads`` x ``dim`` features inside a wider row-major buffer: row s starts at element
+    ``offset + s * stride`` of ``t`` (ops.rs:299-308)."""
+
+    t: torch.Tensor
+    offset: int
+    stride: int
+    tokens: int
+    heads: int
+    dim: int
+
+    def layout(self):
+        return (self.tokens, self.heads, self.dim, self.stride)
+
+    def ptr(self) -> int:
+        """The device address of row 0, after the reference's bounds check (ops.rs:310-323)."""
+        last = self.offset + (max(self.tokens, 1) - 1) * self.stride + self.heads * self.dim
+        if self.stride < self.heads * self.dim or last > self.t.numel():
+            raise H3Error(f"rows of {self.heads} x {self.dim} at offset {self.offset} with stride {self.stride} do not "
+                          f"fit {list(self.t.shape)}")
+        if not self.t.is_contiguous():
+            raise H3Error("rows must live in a contiguous tensor")
+        return self.t.data_ptr() + self.offset * self.t.element_size()
+
+    @staticmethod
+    def qkv(qkv: torch.Tensor, heads: int, dim: int):
+        """q, k, v as the three strided parts of a qkv linear's output [tokens, 3 * heads * dim] (dit.rs:346-350)."""
+        tokens = qkv.shape[0]
+        w = heads * dim
+        return tuple(Rows(qkv, i * w, 3 * w, tokens, heads, dim) for i in range(3))
+
+    @staticmethod
+    def packed(x: torch.Tensor, heads: int, dim: int) -> "Rows":
+        """Rows of a packed [tokens, heads * dim] tensor."""
+        return Rows(x, 0, heads * dim, x.shape[0], heads, dim)
+
+
+def attention(q: Rows, k: Rows, v: Rows, out: torch.Tensor) -> None:
+    """``out = softmax(q . k^T / sqrt(dim)) . v`` per head; out [tokens, heads * dim] (ops.rs:436-461)."""
+    if q.layout() != k.layout() or q.layout() != v.layout():
+        raise H3Error("attention: q, k and v must have the same layout")
+    if out.numel() != q.tokens * q.heads * q.dim:
+        raise H3Error(f"attention: out {list(out.shape)} for {q.tokens} tokens of {q.heads} x {q.dim}")
+    if not out.is_contiguous():
+        raise H3Error("attention: out must be contiguous")
+    ctx = context(out.device)
+    ctx.attention(q.ptr(), k.ptr(), v.ptr(), dt_code(q.t.dtype), q.tokens, q.heads, q.dim, q.stride, out.data_ptr(),
+                  dt_code(out.dtype))
+
+
+def attention_batch(q: Rows, k: Rows, v: Rows, seqs: int, out: torch.Tensor) -> None:
+    """Attention over ``seqs`` independent sequences of ``q.tokens / seqs`` tokens each, in one call (ops.rs:405-434)."""
+    if q.layout() != k.layout() or q.layout() != v.layout():
+        raise H3Error("attention_batch: q, k and v must have the same layout")
+    if seqs == 0 or q.tokens % seqs != 0:
+        raise H3Error(f"attention_batch: {q.tokens} tokens are not {seqs} equal sequences")
+    if out.numel() != q.tokens * q.heads * q.dim:
+        raise H3Error(f"attention_batch: out {list(out.shape)} for {q.tokens} tokens of {q.heads} x {q.dim}")
+    ctx = context(out.device)
+    ctx.attention_batch(q.ptr(), k.ptr(), v.ptr(), dt_code(q.t.dtype), seqs, q.tokens // seqs, q.heads, q.dim, q.stride,
+                        out.data_ptr(), dt_code(out.dtype))

@@ -1,0 +1,202 @@
+"""The CPU oracle pinned: against the reference's own known-answer tests (dtype conversions, engine/h3-core/src/dtype.rs
+:137-155), against an independent numpy restatement of the reference quantiser (kernels/h3sycl.cpp:1733-1761), against
+float64 softmax attention, and against the committed golden fixtures (tests/golden/)."""
+import glob
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def f32(bits_u32):
+    return np.array(bits_u32, np.uint32).view(np.float32)
+
+
+# ---- dtype helpers: the reference's own known answers --------------------------------------------------------------
+def test_bf16_known_answers(orc):
+    # engine/h3-core/src/dtype.rs:145-147: ties go to even
+    assert orc.f32_to_bf16(f32([0x3F808000]))[0] == 0x3F80
+    assert orc.f32_to_bf16(f32([0x3F818000]))[0] == 0x3F82
+    # dtype.rs:139-143: round trip within 0.4 %
+    v = np.array([0.0, 1.0, -1.0, 0.5, 3.140625, -1234.0, 1e-20], np.float32)
+    r = orc.bf16_to_f32(orc.f32_to_bf16(v))
+    assert np.all(np.abs(r - v) <= np.abs(v) * 0.004)
+
+
+def test_f16_known_answers(orc):
+    # engine/h3-core/src/dtype.rs:149-155
+    got = orc.f16_to_f32(np.array([0x3C00, 0xC000, 0x0001, 0x7C00, 0x0000], np.uint16))
+    assert got[0] == 1.0 and got[1] == -2.0 and got[2] == np.float32(5.9604645e-8) and np.isinf(got[3]) and got[4] == 0.0
+
+
+def test_f16_matches_ieee(orc):
+    h = np.arange(65536, dtype=np.uint16)
+    ref = h.view(np.float16).astype(np.float32)
+    got = orc.f16_to_f32(h)
+    ok = ~np.isnan(ref)
+    assert np.array_equal(got.view(np.uint32)[ok], ref.view(np.uint32)[ok]) and np.all(np.isnan(got[~ok]))
+    rng = np.random.default_rng(0)
+    x = (rng.standard_normal(1 << 18) * np.exp(rng.uniform(-25, 12, 1 << 18))).astype(np.float32)
+    x = np.concatenate([x, np.array([65504, 65519.99, 65520, 2.98e-8, 2.9802322e-8, 5.96e-8, -0.0], np.float32)])
+    with np.errstate(over="ignore"):
+        assert np.array_equal(orc.f32_to_f16(x), x.astype(np.float16).view(np.uint16))
+
+
+def test_bf16_matches_rne(orc):
+    rng = np.random.default_rng(1)
+    u = rng.integers(0, 1 << 32, 1 << 18, dtype=np.uint64).astype(np.uint32)
+    u = u[(u & 0x7F800000) != 0x7F800000]
+    got = orc.f32_to_bf16(u.view(np.float32))
+    lsb = (u >> 16) & 1
+    want = ((u.astype(np.uint64) + 0x7FFF + lsb) >> 16).astype(np.uint16)
+    assert np.array_equal(got, want)
+
+
+# ---- the quantiser against an independent numpy restatement ---------------------------------------------------------
+def round_half_away(x):
+    t = np.trunc(x)
+    return t + np.where(np.abs(x - t) >= 0.5, np.sign(x), 0).astype(x.dtype)
+
+
+def np_kmean(kf):
+    return (np.add.accumulate(kf, axis=0, dtype=np.float32)[-1] / np.float32(kf.shape[0])).astype(np.float32)
+
+
+def np_quant(xf, mean, S, H, D):
+    nb = (S + 63) // 64
+    dst = np.zeros((H, S, D), np.int8)
+    sc = np.zeros((H, nb), np.float32)
+    for h in range(H):
+        for b in range(nb):
+            blk = xf[b * 64:(b + 1) * 64, h * D:(h + 1) * D]
+            y = (blk - (mean[h * D:(h + 1) * D] if mean is not None else np.float32(0))).astype(np.float32)
+            m = np.float32(np.max(np.abs(y)))
+            inv = np.float32(127) / m if m > 0 else np.float32(0)
+            sc[h, b] = m / np.float32(127)
+            dst[h, b * 64:b * 64 + blk.shape[0]] = np.clip(round_half_away((y * inv).astype(np.float32)), -127, 127)
+    return dst, sc
+
+
+def to_dt(orc, x, dt):
+    if dt == orc.F16:
+        return orc.f32_to_f16(x), orc.f16_to_f32(orc.f32_to_f16(x))
+    if dt == orc.BF16:
+        return orc.f32_to_bf16(x), orc.bf16_to_f32(orc.f32_to_bf16(x))
+    return x.astype(np.float32), x.astype(np.float32)
+
+
+@pytest.mark.parametrize("S", [1, 63, 64, 65, 200])
+@pytest.mark.parametrize("dt", [1, 2, 0])
+def test_quantiser_matches_numpy(orc, S, dt):
+    H, D = 2, 128
+    st = 3 * H * D + 8
+    rng = np.random.default_rng(S * 10 + dt)
+    x = rng.standard_normal((S, st)).astype(np.float32)
+    x[:, H * D:2 * H * D] += (rng.standard_normal(H * D) * 2).astype(np.float32)
+    raw, val = to_dt(orc, x, dt)
+    kval = np.ascontiguousarray(val[:, H * D:2 * H * D])
+    km = orc.kmean((raw, H * D), dt, S, H, D, st)
+    assert np.array_equal(km.view(np.uint32), np_kmean(kval).view(np.uint32))
+    iq, qs = orc.quant(raw, dt, S, H, D, st)
+    wq, wqs = np_quant(np.ascontiguousarray(val[:, :H * D]), None, S, H, D)
+    assert np.array_equal(iq, wq) and np.array_equal(qs.view(np.uint32), wqs.view(np.uint32))
+    ik, ks = orc.quant((raw, H * D), dt, S, H, D, st, km)
+    wk, wks = np_quant(kval, km, S, H, D)
+    assert np.array_equal(ik, wk) and np.array_equal(ks.view(np.uint32), wks.view(np.uint32))
+
+
+def test_quantiser_edges(orc):
+    """round half away from zero, clamp at +-127 (never -128), an all-zero block gives scale 0 and zeros."""
+    S, H, D = 128, 1, 128
+    x = np.zeros((S, D), np.float32)
+    x[0, 0] = 127.0                        # block 0: m = 127, inv = 1
+    x[0, 1], x[0, 2], x[0, 3], x[0, 4] = 2.5, -2.5, 0.5, -127.0
+    iq, qs = orc.quant(x, orc.F32, S, H, D, D)
+    assert qs[0, 0] == np.float32(1.0) and qs[0, 1] == 0.0
+    assert list(iq[0, 0, :5]) == [127, 3, -3, 1, -127]
+    assert np.all(iq[0, 64:] == 0) and iq.min() >= -127
+
+
+def test_prepass_layout(orc):
+    """sc = q scales [H, nb] | k scales [H, nb] | k mean [H*D] (kernels/h3sycl.cpp:1716-1718)."""
+    S, H, D = 130, 2, 128
+    rng = np.random.default_rng(3)
+    raw = orc.f32_to_f16(rng.standard_normal((S, 3 * H * D)).astype(np.float32))
+    iq, ik, qs, ks, km, hv = orc.sage_prepass(raw, (raw, H * D), (raw, 2 * H * D), orc.F16, S, H, D, 3 * H * D)
+    assert qs.shape == (H, 3) and ks.shape == (H, 3) and km.shape == (H * D,)
+    assert np.array_equal(hv[1, 5], raw[5, 2 * H * D + D:2 * H * D + 2 * D])
+    assert np.array_equal(km, orc.kmean((raw, H * D), orc.F16, S, H, D, 3 * H * D))
+
+
+# ---- attention semantics against float64 ----------------------------------------------------------------------------
+def _qkv(S, H, D, seed):
+    from sycl_minimax_h3_b200.workloads import bits, make_qkv
+
+    return bits(make_qkv(S, H, D, seed=seed))
+
+
+@pytest.mark.parametrize("S", [1, 65, 384])
+def test_sage_and_sdpa_semantics_vs_exact(orc, S):
+    H, D = 2, 128
+    host = _qkv(S, H, D, seed=S)
+    st = 3 * H * D
+    rh, rs = np.repeat(np.arange(H), S), np.tile(np.arange(S), H)
+    exact = orc.exact_rows(host, (host, H * D), (host, 2 * H * D), orc.F16, S, H, D, st, rh, rs)
+    iq, ik, qs, ks, km, hv = orc.sage_prepass(host, (host, H * D), (host, 2 * H * D), orc.F16, S, H, D, st)
+    sage = orc.sage_rows(iq, ik, hv, qs, ks, S, H, D, rh, rs).view(np.float16).astype(np.float32)
+    sdpa = orc.sdpa_rows(host, (host, H * D), (host, 2 * H * D), orc.F16, S, H, D, st, rh, rs).view(np.float16).astype(np.float32)
+    assert orc.row_cosines(sage, exact).min() >= 0.999
+    assert orc.row_cosines(sdpa, exact).min() >= 0.9999
+    rel, cos = orc.compare(sdpa, exact)
+    assert rel < 1e-2 and cos > 0.9999
+
+
+def test_dispatch_threshold(orc):
+    """h3s_attention: Sage at S >= sage_min_s, fp16 SDPA below (kernels/h3sycl.cpp:1784)."""
+    S, H, D = 96, 2, 128
+    host = _qkv(S, H, D, seed=11)
+    st = 3 * H * D
+    rh, rs = np.repeat(np.arange(H), S), np.tile(np.arange(S), H)
+    a_sdpa = orc.attention(host, (host, H * D), (host, 2 * H * D), orc.F16, S, H, D, st, orc.F16, sage_min_s=S + 1)
+    a_sage = orc.attention(host, (host, H * D), (host, 2 * H * D), orc.F16, S, H, D, st, orc.F16, sage_min_s=S)
+    want_sdpa = orc.sdpa_rows(host, (host, H * D), (host, 2 * H * D), orc.F16, S, H, D, st, rh, rs)
+    assert np.array_equal(a_sdpa.reshape(S, H, D).transpose(1, 0, 2).reshape(H * S, D), want_sdpa)
+    assert not np.array_equal(a_sage, a_sdpa)
+    with pytest.raises(ValueError):
+        orc.attention(host, host, host, orc.F16, S, H, D, H * D - 1)
+
+
+def test_out_dtypes_round_through_half(orc):
+    S, H, D = 40, 1, 128
+    host = _qkv(S, H, D, seed=2)
+    args = (host, (host, H * D), (host, 2 * H * D), orc.F16, S, H, D, 3 * H * D)
+    o16 = orc.attention(*args, out_dt=orc.F16, sage_min_s=1 << 30)
+    o32 = orc.attention(*args, out_dt=orc.F32, sage_min_s=1 << 30)
+    obf = orc.attention(*args, out_dt=orc.BF16, sage_min_s=1 << 30)
+    assert np.array_equal(o32, o16.view(np.float16).astype(np.float32))
+    assert np.array_equal(obf, orc.f32_to_bf16(o16.view(np.float16).astype(np.float32)))
+
+
+# ---- golden fixtures --------------------------------------------------------------------------------------------------
+FIXTURES = sorted(glob.glob(os.path.join(GOLDEN, "*.npz")))
+
+
+def test_golden_fixtures_exist():
+    assert FIXTURES, "tests/golden/*.npz missing (tests/golden/make_golden.py writes them)"
+
+
+@pytest.mark.parametrize("path", FIXTURES, ids=[os.path.basename(p) for p in FIXTURES])
+def test_golden_fixture(orc, path):
+    import sys
+
+    sys.path.insert(0, GOLDEN)
+    import make_golden
+
+    f = np.load(path)
+    got = make_golden.compute(orc, f)
+    for key, want in got.items():
+        assert np.array_equal(np.asarray(f[key]).view(np.uint8), np.asarray(want).view(np.uint8)), f"{path}: {key} differs"
