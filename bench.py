@@ -166,6 +166,8 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--quick", action="store_true", help="main workload only (no c1/c2/c4 side numbers)")
+    ap.add_argument("--S", type=int, default=47232, help="tokens of the main workload (profiling runs use a smaller case)")
+    ap.add_argument("--H", type=int, default=32, help="heads of the main workload")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -200,7 +202,7 @@ def main() -> None:
 
     peaks = measured_peaks()
     D = 128
-    S, H = 47232, 32
+    S, H = args.S, args.H
     if H % world:
         raise SystemExit(f"{H} heads do not split over {world} GPUs")
     h = H // world
@@ -380,8 +382,9 @@ def main() -> None:
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_call, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int8+fp16", "data": DATA,
-            "config": {"workload": "c3: 32 heads x 47,232 tokens x 128 per call, Sage path, fp16 q/k/v inside a qkv buffer "
-                                   "(row stride 3*H*D), fp16 out; 50 fresh blocks",
+            "config": {"workload": (f"c3: {H} heads x {S:,} tokens x 128 per call" if (S, H) == (47232, 32) else
+                                    f"profiling case: {H} heads x {S:,} tokens x 128 per call") +
+                                   ", Sage path, fp16 q/k/v inside a qkv buffer (row stride 3*H*D), fp16 out; fresh blocks",
                        "S": S, "H": H, "D": D, "blocks": min(nblocks, args.warmup + args.steps),
                        "parallelism": f"heads/{world}" if world > 1 else "1 GPU",
                        "l2": "inputs larger than L2 (1.16 GB per block), a different block every step"},

@@ -103,6 +103,66 @@ __device__ __forceinline__ void tma_rows(void* dst, const CUtensorMap* map, uint
     else tma_load_4d(dst, map, bar, c0, row, head, seq);
 }
 
+
+// The epilogue of one query row: O (fp32, 128 TMEM columns from o_taddr) / l, rounded to half, then to out_dt
+// (kernels/h3sycl.cpp:1769-1771), stored at out + b*out_seq + qrow*out_tok + h*out_head. Warp-collective (TMEM loads):
+// every lane calls it; rows past S (live = false) load but do not store.
+__device__ __forceinline__ void store_out_row(const AttnArgs& a, int b, int h, int qrow, uint32_t o_taddr, float inv, bool live) {
+    const long long base = (long long) b * a.out_seq + (long long) qrow * a.out_tok + (long long) h * a.out_head;
+#pragma unroll
+    for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t o[32];
+        tmem_ld32(o_taddr + c4 * 32, o);
+        tmem_wait_ld();
+        if (!live) continue;
+        __half hv[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) hv[i] = __float2half_rn(__uint_as_float(o[i]) * inv);
+        const long long e0 = base + c4 * 32;
+        if (a.out_dt == F16) {
+            __half* dst = reinterpret_cast<__half*>(a.out) + e0;
+            if (a.out_vec) {
+#pragma unroll
+                for (int v = 0; v < 4; ++v) reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(hv)[v];
+            } else {
+                for (int i = 0; i < 32; ++i) dst[i] = hv[i];
+            }
+        } else if (a.out_dt == BF16) {
+            __nv_bfloat16 bv[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) bv[i] = __float2bfloat16_rn(__half2float(hv[i]));
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) + e0;
+            if (a.out_vec) {
+#pragma unroll
+                for (int v = 0; v < 4; ++v) reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(bv)[v];
+            } else {
+                for (int i = 0; i < 32; ++i) dst[i] = bv[i];
+            }
+        } else {
+            float fv[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) fv[i] = __half2float(hv[i]);
+            float* dst = reinterpret_cast<float*>(a.out) + e0;
+            if (a.out_vec) {
+#pragma unroll
+                for (int v = 0; v < 8; ++v) reinterpret_cast<float4*>(dst)[v] = reinterpret_cast<const float4*>(fv)[v];
+            } else {
+                for (int i = 0; i < 32; ++i) dst[i] = fv[i];
+            }
+        }
+    }
+}
+
+// max of 32 values with three-input max instructions (a tree: 16 instructions, depth 4)
+__device__ __forceinline__ float max32(const uint32_t (&r)[32]) {
+    float m[11];
+#pragma unroll
+    for (int i = 0; i < 10; ++i) m[i] = fmax3(__uint_as_float(r[3 * i]), __uint_as_float(r[3 * i + 1]), __uint_as_float(r[3 * i + 2]));
+    m[10] = fmaxf(__uint_as_float(r[30]), __uint_as_float(r[31]));
+    const float a0 = fmax3(m[0], m[1], m[2]), a1 = fmax3(m[3], m[4], m[5]), a2 = fmax3(m[6], m[7], m[8]);
+    return fmax3(fmax3(a0, a1, a2), m[9], m[10]);
+}
+
 template <bool I8>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_fwd(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -279,7 +339,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 c_hi = cq * a.ks[(size_t) h * a.nb + b1];
             }
             const int kv0 = j * kTileN;
-            float mt = -INFINITY;
 #pragma unroll
             for (int c4 = 0; c4 < 4; ++c4)
 #pragma unroll
@@ -287,10 +346,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     float f;
                     if constexpr (I8) f = (float) (int) r[c4][i] * (c4 < 2 ? c_lo : c_hi);
                     else f = __uint_as_float(r[c4][i]) * cq;
-                    if (kv0 + c4 * 32 + i >= S) f = -INFINITY;
                     r[c4][i] = __float_as_uint(f);
-                    mt = fmaxf(mt, f);
                 }
+            if (kv0 + kTileN > S) {                  // the last tile: keys past S do not count
+#pragma unroll
+                for (int c4 = 0; c4 < 4; ++c4)
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (kv0 + c4 * 32 + i >= S) r[c4][i] = __float_as_uint(-INFINITY);
+            }
+            const float mt = fmax3(max32(r[0]), max32(r[1]), fmaxf(max32(r[2]), max32(r[3])));
             const float m_new = fmaxf(m_run, mt);
             const bool grow = m_new > m_run + 8.0f;  // first tile: m_run = -inf
             float alpha = 1.0f;
@@ -305,7 +370,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                 if (!ok) break;
             }
             uint8_t* pt = sm + C::OFF_P + (j % C::NP) * C::P_BYTES;
-            float sum = 0.0f;
+            float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int c = 0; c < 16; ++c) {          // 16-byte chunks of 8 keys
                 uint32_t pk[4];
@@ -314,14 +379,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                     const int i = c * 8 + 2 * e;
                     const float p0 = ex2(__uint_as_float(r[i >> 5][i & 31]) - m_run);
                     const float p1 = ex2(__uint_as_float(r[(i + 1) >> 5][(i + 1) & 31]) - m_run);
-                    sum += p0 + p1;
+                    sum[2 * e] += p0;
+                    sum[2 * e + 1] += p1;
                     pk[e] = pack_half2(p0, p1);
                 }
                 const int cb = c >> 3, ch = c & 7;
                 uint4* dst = reinterpret_cast<uint4*>(pt + cb * C::CB_BYTES + row * 128 + ((ch ^ (row & 7)) << 4));
                 *dst = make_uint4(pk[0], pk[1], pk[2], pk[3]);
             }
-            l_run += sum;
+            l_run += ((sum[0] + sum[1]) + (sum[2] + sum[3])) + ((sum[4] + sum[5]) + (sum[6] + sum[7]));
             // rescale O (which holds the sum up to tile j-1) in place when this row's max grew
             if (__any_sync(0xffffffffu, grow && j > 0)) {
                 if (C::NP != 1) {
@@ -350,51 +416,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             if (lane == 0) fail(kErrSoftmax);
         } else {
             tc_fence_after();
-            const float inv = 1.0f / l_run;
-            const bool live = qrow < S;
-            const long long base = (long long) b * a.out_seq + (long long) qrow * a.out_tok + (long long) h * a.out_head;
-#pragma unroll
-            for (int c4 = 0; c4 < 4; ++c4) {
-                uint32_t o[32];
-                tmem_ld32(t_lane + kColO + c4 * 32, o);
-                tmem_wait_ld();
-                if (!live) continue;
-                __half hv[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) hv[i] = __float2half_rn(__uint_as_float(o[i]) * inv);
-                const long long e0 = base + c4 * 32;
-                if (a.out_dt == F16) {
-                    __half* dst = reinterpret_cast<__half*>(a.out) + e0;
-                    if (a.out_vec) {
-#pragma unroll
-                        for (int v = 0; v < 4; ++v) reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(hv)[v];
-                    } else {
-                        for (int i = 0; i < 32; ++i) dst[i] = hv[i];
-                    }
-                } else if (a.out_dt == BF16) {
-                    __nv_bfloat16 bv[32];
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) bv[i] = __float2bfloat16_rn(__half2float(hv[i]));
-                    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) + e0;
-                    if (a.out_vec) {
-#pragma unroll
-                        for (int v = 0; v < 4; ++v) reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(bv)[v];
-                    } else {
-                        for (int i = 0; i < 32; ++i) dst[i] = bv[i];
-                    }
-                } else {
-                    float fv[32];
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) fv[i] = __half2float(hv[i]);
-                    float* dst = reinterpret_cast<float*>(a.out) + e0;
-                    if (a.out_vec) {
-#pragma unroll
-                        for (int v = 0; v < 8; ++v) reinterpret_cast<float4*>(dst)[v] = reinterpret_cast<const float4*>(fv)[v];
-                    } else {
-                        for (int i = 0; i < 32; ++i) dst[i] = fv[i];
-                    }
-                }
-            }
+            store_out_row(a, b, h, qrow, t_lane + kColO, 1.0f / l_run, qrow < S);
         }
     }
 

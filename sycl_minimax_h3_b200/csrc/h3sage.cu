@@ -1,6 +1,6 @@
 // h3sage.cu - libh3sage.so: SageAttention v1 for libh3cuda.so, the plugin interface of the reference's kernels/sage.cpp
-// (maxfridbe/sycl_minimax_h3) on sm_100a. The kernel is attn_fwd<true> (attn.cuh): int8 Q.K^T on tcgen05 kind::i8,
-// dequantised with the per-block scales, online softmax, P.V in half on kind::f16.
+// (maxfridbe/sycl_minimax_h3) on sm_100a. The kernel is attn_sage2 (attn2.cuh): int8 Q.K^T on tcgen05 kind::i8,
+// dequantised with the per-block scales, online softmax, P.V in half on kind::f16, two 128-row query tiles per CTA.
 //
 // The reference's plugin wraps Intel's ARK kernel (kernels/sage.cpp:51-52) and its g_err is a process global
 // (kernels/sage.cpp:23); so is this one's.
@@ -12,7 +12,7 @@
 #include <string>
 
 #include "../../include/h3sage.h"
-#include "attn.cuh"
+#include "attn2.cuh"
 
 namespace {
 
@@ -78,7 +78,7 @@ int run(cudaStream_t st, const int8_t* q, const int8_t* k, const void* v, int64_
     a.v_order = v_order;
     a.err = err;
     a.wait_ns = wait_ns ? wait_ns : kDefaultWaitNs;
-    const cudaError_t ce = h3::launch_attn<true>(mq, mk, mv, a, 1, st);
+    const cudaError_t ce = h3::launch_sage2(mq, mk, mv, a, st);
     if (ce != cudaSuccess) return fail(std::string("h3sage: launch: ") + cudaGetErrorString(ce));
     return 0;
 }

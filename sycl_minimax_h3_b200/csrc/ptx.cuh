@@ -150,6 +150,13 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// three-input max (sm_100): halves the instructions of a max reduction
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 // ---- UMMA descriptors ----------------------------------------------------------------------------------------------
 // Shared-memory matrix descriptor: start address, leading / stride byte offsets (all >> 4), version 1 (sm_100),
 // base offset 0 (atoms 1024-byte aligned), layout type in bits 61-63 (2 = 128-byte swizzle).
