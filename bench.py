@@ -241,6 +241,8 @@ def main() -> None:
         e1.record(stream)
         torch.cuda.synchronize()
     ctx.wait()
+    if not bool(torch.isfinite(out).all()):
+        raise SystemExit("bench: the timed attention produced non-finite values; no number is reported")
     barrier()
     ms_total = max_over_ranks(e0.elapsed_time(e1))
     ms_call = ms_total / args.steps
@@ -285,7 +287,7 @@ def main() -> None:
     achieved = ops_per_call(S, h, D) / (ms_kernel / 1e3) / 1e12
     roofline = {"bound": "tensor", "achieved": achieved, "peak": mixed_peak, "unit": "TFLOP/s",
                 "frac": achieved / mixed_peak, "traffic": None,
-                "kernel": "attn_fwd<true> (Sage int8 QK^T + fp16 PV, tcgen05)",
+                "kernel": "attn_sage2 (Sage int8 QK^T + fp16 PV, tcgen05, 2 query tiles per CTA)",
                 "peak_basis": f"4/3 x {peaks['source']} bf16 {peaks['bf16_tflops']} TFLOP/s: int8 QK^T at 2x, fp16 PV at 1x",
                 "ms_per_launch": ms_kernel,
                 "pct_int8_peak_measured_x2": achieved / (2 * peaks["bf16_tflops"]),
