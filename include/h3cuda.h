@@ -109,6 +109,22 @@ void* h3s_stream(void* ctx);
  * It faults nothing and leaves the context usable. */
 int h3s_selftest_wait_timeout(void* ctx, uint64_t wait_ns);
 
+/* The int8 Sage attention with no device allocation at all. No counterpart in the reference. For callers that cannot
+ * allocate device memory when they call: code on a path that must not synchronise the device (cudaMalloc and cudaFree
+ * may), and hosts whose device memory is wholly owned and budgeted by another allocator (a fixed cap, a caching
+ * allocator), where a library allocating behind their back breaks the budget.
+ * It computes what h3s_attention computes on its Sage path (K channel mean, int8 q/k per 64-row block, the tcgen05
+ * kernel) for fp16 q, k, v rows at `stride` (16-byte aligned starts, stride a multiple of 8), D = 128, into out
+ * [S, H*D] in out_dt, queued on *stream (stream points to a cudaStream_t; NULL: the legacy default stream). Its scratch
+ * is a fixed array of 8 MiB + 128 KiB inside this library, which every GPU that loads the library holds until the
+ * process exits: S*H*D <= 4,194,304 and H*D <= 16,384, else -1 with the limit in h3s_last_error(). The first call on
+ * a device looks the array's address up (cudaGetSymbolAddress); make that first call before any stream capture.
+ * err: a device int of the caller; each call first sets it to 0 on the stream, and a kernel whose wait gives up ORs a
+ * nonzero code into it. Each GPU has its own copy of the array, shared by every call on that GPU: two calls on one GPU
+ * whose work overlaps (different streams, not ordered by events) race on it, so order them. */
+int h3s_attention_sage_static(void* stream, const void* q, const void* k, const void* v, int64_t S, int64_t H, int64_t D,
+                              int64_t stride, void* out, int out_dt, int* err);
+
 #ifdef __cplusplus
 }
 #endif

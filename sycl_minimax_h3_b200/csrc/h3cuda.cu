@@ -27,6 +27,7 @@
 #include "../../include/h3sage.h"
 #include "attn.cuh"
 #include "prepass.cuh"
+#include "attn2.cuh"
 
 namespace {
 
@@ -411,6 +412,34 @@ __global__ void wait_timeout_kernel(int* err, unsigned long long wait_ns) {
     __syncthreads();
 }
 
+// ---- the allocation-free Sage path (h3s_attention_sage_static) -------------------------------------------------------
+// For callers that cannot allocate device memory when they call: code on a path that must not synchronise the device
+// (cudaMalloc / cudaFree may), and hosts whose device memory is wholly owned and budgeted by another allocator. Its
+// scratch (the int8 q and k and their scales) lives in this fixed array instead, which every GPU that loads this
+// library holds until the process exits. Each GPU has its own copy; calls on one GPU share it, so overlapping calls
+// race. The first call on a device looks the address up (cudaGetSymbolAddress), before any stream capture.
+constexpr size_t kStaticMaxElems = size_t(4) << 20;           // S * H * D of one call, at most
+constexpr size_t kStaticMaxHD = 16384;                          // H * D of one call, at most
+constexpr size_t kStaticScaleBytes = 128 << 10;                 // q scales, k scales, k mean
+constexpr size_t kStaticBytes = 2 * kStaticMaxElems + kStaticScaleBytes;
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticBytes];
+
+std::mutex g_static_mu;
+uint8_t* g_static_ptr[64] = {};                                 // the array's device address, per device
+
+// The device address of the scratch array on the current device (cudaGetSymbolAddress once per device).
+uint8_t* static_scratch(int dev) {
+    if (dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> l(g_static_mu);
+    if (!g_static_ptr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
+        if (e != cudaSuccess) { cuda_fail("cudaGetSymbolAddress", e); return nullptr; }
+        g_static_ptr[dev] = static_cast<uint8_t*>(p);
+    }
+    return g_static_ptr[dev];
+}
+
 }  // namespace
 
 extern "C" {
@@ -674,6 +703,93 @@ int h3s_selftest_wait_timeout(void* ctx, uint64_t wait_ns) {
     wait_timeout_kernel<<<1, 32, 0, c.st>>>(c.err, (unsigned long long) wait_ns);
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : cuda_fail("h3s_selftest_wait_timeout", e);
+}
+
+int h3s_attention_sage_static(void* stream, const void* q, const void* k, const void* v, int64_t S, int64_t H, int64_t D,
+                              int64_t stride, void* out, int out_dt, int* err) {
+    if (S <= 0 || H <= 0 || D <= 0) return 0;
+    if (D != 128) { g_err = "h3s_attention_sage_static: head size " + std::to_string(D) + " (128 only)"; return -1; }
+    if (stride < H * D) { g_err = "h3s_attention_sage_static: the row stride is shorter than a row"; return -1; }
+    if ((size_t) S * H * D > kStaticMaxElems || (size_t) (H * D) > kStaticMaxHD) {
+        g_err = "h3s_attention_sage_static: S*H*D = " + std::to_string(S * H * D) + ", H*D = " + std::to_string(H * D) +
+                " is beyond the fixed scratch (S*H*D <= " + std::to_string(kStaticMaxElems) + ", H*D <= " +
+                std::to_string(kStaticMaxHD) + ")";
+        return -1;
+    }
+    if (!check_dt(out_dt)) { g_err = "h3s_attention_sage_static: unknown output type"; return -1; }
+    if (!err) { g_err = "h3s_attention_sage_static: err must be a device int of the caller"; return -1; }
+    if (!aligned16(q) || !aligned16(k) || !aligned16(v) || (stride * 2) % 16 != 0) {
+        g_err = "h3s_attention_sage_static: q, k, v must start on 16 bytes and the row stride be a multiple of 8";
+        return -1;
+    }
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail("h3s_attention_sage_static", e);
+    uint8_t* base = static_scratch(dev);
+    if (!base) return -1;
+    cudaStream_t st = stream ? *static_cast<cudaStream_t*>(stream) : nullptr;
+    const int64_t nb = (S + kSageBlock - 1) / kSageBlock;    // H*nb <= S*H/64 + H <= 640: the scales fit 128 KiB
+    int8_t* iq = reinterpret_cast<int8_t*>(base);
+    int8_t* ik = reinterpret_cast<int8_t*>(base + kStaticMaxElems);
+    float* sc = reinterpret_cast<float*>(base + 2 * kStaticMaxElems);
+    float* qs = sc;
+    float* ks = sc + H * nb;
+    float* kmean = sc + 2 * H * nb;
+    const int C = (int) (H * D);
+    // the caller's error word starts each call at zero (a set word makes the attention kernel skip its work)
+    if ((e = cudaMemsetAsync(err, 0, sizeof(int), st)) != cudaSuccess) return cuda_fail("h3s_attention_sage_static", e);
+    // K mean (one chain per channel), then the two quantisers, all on the caller's stream
+    CUtensorMap map;
+    auto enc = tensor_map_encoder();
+    bool tma = false;
+    if (enc) {
+        const cuuint64_t dims[2] = {(cuuint64_t) C, (cuuint64_t) S};
+        const cuuint64_t strides[1] = {(cuuint64_t) (stride * 2)};
+        const cuuint32_t box[2] = {(cuuint32_t) kMeanCh, (cuuint32_t) kMeanRows};
+        const cuuint32_t estr[2] = {1, 1};
+        tma = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(k), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    }
+    const uint64_t wait_ns = 2000000000ull;
+    if (tma) {
+        using M = MeanCfg<F16>;
+        if ((e = cudaFuncSetAttribute(kmean_tma<F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, M::SMEM)) != cudaSuccess)
+            return cuda_fail("h3s_attention_sage_static", e);
+        kmean_tma<F16><<<(C + kMeanCh - 1) / kMeanCh, kMeanThreads, M::SMEM, st>>>(map, (int) S, C, kmean, err, wait_ns);
+    } else {
+        kmean_plain<F16><<<(C + 127) / 128, 128, 0, st>>>(k, (int) S, C, (long long) stride, kmean);
+    }
+    const dim3 grid((unsigned) nb, (unsigned) H);
+    quant_rows<F16, 128, true><<<grid, kQuantThreads, 0, st>>>(q, (int) S, stride, nullptr, iq, qs, (int) nb);
+    quant_rows<F16, 128, true><<<grid, kQuantThreads, 0, st>>>(k, (int) S, stride, kmean, ik, ks, (int) nb);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("h3s_attention_sage_static", e);
+    // the int8 attention, v read in place, out written in place
+    CUtensorMap mq, mk, mv;
+    std::string me = make_rows_map(&mq, iq, true, D, S, H, 1, D, S * D, H * S * D, 0);
+    if (me.empty()) me = make_rows_map(&mk, ik, true, D, S, H, 1, D, S * D, H * S * D, 0);
+    if (me.empty()) me = make_rows_map(&mv, v, false, D, S, H, 1, stride * 2, D * 2, 0, 1);
+    if (!me.empty()) { g_err = "h3s_attention_sage_static: " + me; return -1; }
+    AttnArgs a{};
+    a.S = (int) S;
+    a.H = (int) H;
+    a.n_kv = (int) ((S + kTileN - 1) / kTileN);
+    a.scale_log2 = (1.0f / std::sqrt((float) D)) * 1.4426950408889634f;
+    a.qs = qs;
+    a.ks = ks;
+    a.nb = (int) nb;
+    a.blk = kSageBlock;
+    a.out = out;
+    a.out_tok = H * D;
+    a.out_head = D;
+    a.out_dt = out_dt;
+    a.out_vec = aligned16(out) ? 1 : 0;
+    a.q_order = a.k_order = 0;
+    a.v_order = 1;
+    a.err = err;
+    a.wait_ns = wait_ns;
+    if ((e = launch_sage2(mq, mk, mv, a, st)) != cudaSuccess) return cuda_fail("h3s_attention_sage_static", e);
+    return 0;
 }
 
 }  // extern "C"

@@ -45,6 +45,7 @@ CUDA_SYMBOLS = [
     ("h3s_sage_prepass", I, [P, P, P, I, I64, I64, I64, I64, P, P, P]),
     ("h3s_stream", P, [P]),
     ("h3s_selftest_wait_timeout", I, [P, U64]),
+    ("h3s_attention_sage_static", I, [P, P, P, P, I64, I64, I64, I64, P, I, P]),
 ]
 # every entry point of include/h3sage.h
 SAGE_SYMBOLS = [
