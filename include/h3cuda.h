@@ -17,6 +17,8 @@
  *   H3S_POISON                 fill new buffers with 0xff bytes (NaN) to expose reads of unwritten memory
  *   H3S_WAIT_MS                limit of every wait inside a kernel (default 2000); past it the kernel stops and
  *                              h3s_wait reports the failure
+ *   H3S_SAGE_KERNEL=2          run the earlier Sage kernel (attn_sage2) instead of attn_sage3, for comparison
+ *                              (read once per process; libh3sage.so reads it too)
  */
 #ifndef H3CUDA_H
 #define H3CUDA_H

@@ -196,40 +196,73 @@ void orc_sage_prepass(const void* q, const void* k, const void* v, int dt, int64
 // ---- Sage core (kernels/sage.cpp:41-52 semantics) on selected (head, row) pairs --------------------------------------
 // iq, ik int8 [H, S, D]; hv half [H, S, D]; qs, ks [H, nb] for 64-row blocks; out half bits [n, D] for the n pairs
 // (rows_h[i], rows_s[i]). score = (float) dot * (qs * ks * scale); fp32 softmax with the row max; p rounded to half;
-// fp32 sum of p * v; divided by the fp32 sum of p; rounded to half.
-void orc_sage_rows(const int8_t* iq, const int8_t* ik, const uint16_t* hv, const float* qs, const float* ks, int64_t S,
-                   int64_t H, int64_t D, float scale, const int64_t* rows_h, const int64_t* rows_s, int64_t n,
-                   uint16_t* out) {
-    (void) H;
+// fp32 sum of p * v; divided by the fp32 sum of p; rounded to half. The rows are taken head by head, with that head's v
+// widened to float once; the per-element order of every sum is the same as the plain loops'.
+}  // extern "C"
+
+namespace {
+template <int DC>
+inline int32_t dot_i8(const int8_t* __restrict a, const int8_t* __restrict b, int64_t D) {
+    int32_t acc = 0;
+    const int64_t n = DC > 0 ? DC : D;
+    for (int64_t d = 0; d < n; ++d) acc += (int32_t) a[d] * (int32_t) b[d];
+    return acc;
+}
+template <int DC>
+inline void axpy(float* __restrict o, float p, const float* __restrict v, int64_t D) {
+    const int64_t n = DC > 0 ? DC : D;
+    for (int64_t d = 0; d < n; ++d) o[d] += p * v[d];
+}
+template <int DC>
+void sage_rows_impl(const int8_t* iq, const int8_t* ik, const uint16_t* hv, const float* qs, const float* ks, int64_t S,
+                    int64_t H, int64_t D, float scale, const int64_t* rows_h, const int64_t* rows_s, int64_t n,
+                    uint16_t* out) {
     const int64_t nb = (S + kBlock - 1) / kBlock;
+    std::vector<std::vector<int64_t>> by_head((size_t) H);
+    for (int64_t i = 0; i < n; ++i) by_head[(size_t) rows_h[i]].push_back(i);
     const int nt = threads();
     std::vector<std::vector<float>> s_t((size_t) nt, std::vector<float>((size_t) S)), o_t((size_t) nt, std::vector<float>((size_t) D));
-    par_for(n, 1, [&](int64_t i, int t) {
-        std::vector<float>& s = s_t[(size_t) t];
-        std::vector<float>& o = o_t[(size_t) t];
-        const int64_t h = rows_h[i], r = rows_s[i];
-        const int8_t* qr = iq + (h * S + r) * D;
-        const float cq = qs[h * nb + r / kBlock];
-        float m = -INFINITY;
-        for (int64_t j = 0; j < S; ++j) {
-            const int8_t* kr = ik + (h * S + j) * D;
-            int32_t acc = 0;
-            for (int64_t d = 0; d < D; ++d) acc += (int32_t) qr[d] * (int32_t) kr[d];
-            s[(size_t) j] = (float) acc * (cq * ks[h * nb + j / kBlock] * scale);
-            m = std::max(m, s[(size_t) j]);
-        }
-        std::fill(o.begin(), o.end(), 0.0f);
-        float l = 0.0f;
-        for (int64_t j = 0; j < S; ++j) {
-            const float p = std::exp(s[(size_t) j] - m);
-            l += p;
-            const float ph = half_round(p);
-            const uint16_t* vr = hv + (h * S + j) * D;
-            for (int64_t d = 0; d < D; ++d) o[(size_t) d] += ph * f16_to_f32(vr[d]);
-        }
-        for (int64_t d = 0; d < D; ++d) out[i * D + d] = f32_to_f16(o[(size_t) d] / l);
-    });
+    std::vector<float> vf;
+    for (int64_t h = 0; h < H; ++h) {
+        const std::vector<int64_t>& rows = by_head[(size_t) h];
+        if (rows.empty()) continue;
+        vf.resize((size_t) (S * D));
+        par_for(S, 256, [&](int64_t j, int) {
+            for (int64_t d = 0; d < D; ++d) vf[(size_t) (j * D + d)] = f16_to_f32(hv[(h * S + j) * D + d]);
+        });
+        par_for((int64_t) rows.size(), 1, [&](int64_t ri, int t) {
+            const int64_t i = rows[(size_t) ri], r = rows_s[i];
+            std::vector<float>& s = s_t[(size_t) t];
+            std::vector<float>& o = o_t[(size_t) t];
+            const int8_t* qr = iq + (h * S + r) * D;
+            const float cq = qs[h * nb + r / kBlock];
+            float m = -INFINITY;
+            for (int64_t j = 0; j < S; ++j) {
+                const int32_t acc = dot_i8<DC>(qr, ik + (h * S + j) * D, D);
+                s[(size_t) j] = (float) acc * (cq * ks[h * nb + j / kBlock] * scale);
+                m = std::max(m, s[(size_t) j]);
+            }
+            std::fill(o.begin(), o.end(), 0.0f);
+            float l = 0.0f;
+            for (int64_t j = 0; j < S; ++j) {
+                const float p = std::exp(s[(size_t) j] - m);
+                l += p;
+                axpy<DC>(o.data(), half_round(p), vf.data() + j * D, D);
+            }
+            for (int64_t d = 0; d < D; ++d) out[i * D + d] = f32_to_f16(o[(size_t) d] / l);
+        });
+    }
 }
+}  // namespace
+
+extern "C" void orc_sage_rows(const int8_t* iq, const int8_t* ik, const uint16_t* hv, const float* qs, const float* ks,
+                              int64_t S, int64_t H, int64_t D, float scale, const int64_t* rows_h, const int64_t* rows_s,
+                              int64_t n, uint16_t* out) {
+    if (D == 128) sage_rows_impl<128>(iq, ik, hv, qs, ks, S, H, D, scale, rows_h, rows_s, n, out);
+    else sage_rows_impl<0>(iq, ik, hv, qs, ks, S, H, D, scale, rows_h, rows_s, n, out);
+}
+
+extern "C" {
 
 // ---- fp16 fused SDPA semantics (kernels/h3sycl.cpp:1464-1500, oneDNN graph) on selected (head, row) pairs -------------
 // q, k, v in dt, token rows at `stride`; each value goes through half first (the reference copies q, k, v to half,

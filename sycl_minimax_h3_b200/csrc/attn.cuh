@@ -104,9 +104,48 @@ __device__ __forceinline__ void tma_rows(void* dst, const CUtensorMap* map, uint
 }
 
 
-// The epilogue of one query row: O (fp32, 128 TMEM columns from o_taddr) / l, rounded to half, then to out_dt
-// (kernels/h3sycl.cpp:1769-1771), stored at out + b*out_seq + qrow*out_tok + h*out_head. Warp-collective (TMEM loads):
-// every lane calls it; rows past S (live = false) load but do not store.
+// 32 consecutive output features of one row (fp32 values already divided by the row sum), rounded to half, then to
+// out_dt (kernels/h3sycl.cpp:1769-1771), stored at out + e0 elements.
+__device__ __forceinline__ void store_out32(const AttnArgs& a, long long e0, const float (&val)[32]) {
+    __half hv[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) hv[i] = __float2half_rn(val[i]);
+    if (a.out_dt == F16) {
+        __half* dst = reinterpret_cast<__half*>(a.out) + e0;
+        if (a.out_vec) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(hv)[v];
+        } else {
+            for (int i = 0; i < 32; ++i) dst[i] = hv[i];
+        }
+    } else if (a.out_dt == BF16) {
+        __nv_bfloat16 bv[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) bv[i] = __float2bfloat16_rn(__half2float(hv[i]));
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) + e0;
+        if (a.out_vec) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(bv)[v];
+        } else {
+            for (int i = 0; i < 32; ++i) dst[i] = bv[i];
+        }
+    } else {
+        float fv[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) fv[i] = __half2float(hv[i]);
+        float* dst = reinterpret_cast<float*>(a.out) + e0;
+        if (a.out_vec) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v) reinterpret_cast<float4*>(dst)[v] = reinterpret_cast<const float4*>(fv)[v];
+        } else {
+            for (int i = 0; i < 32; ++i) dst[i] = fv[i];
+        }
+    }
+}
+
+// The epilogue of one query row: O (fp32, 128 TMEM columns from o_taddr) / l, stored at
+// out + b*out_seq + qrow*out_tok + h*out_head. Warp-collective (TMEM loads): every lane calls it; rows past S
+// (live = false) load but do not store.
 __device__ __forceinline__ void store_out_row(const AttnArgs& a, int b, int h, int qrow, uint32_t o_taddr, float inv, bool live) {
     const long long base = (long long) b * a.out_seq + (long long) qrow * a.out_tok + (long long) h * a.out_head;
 #pragma unroll
@@ -115,41 +154,10 @@ __device__ __forceinline__ void store_out_row(const AttnArgs& a, int b, int h, i
         tmem_ld32(o_taddr + c4 * 32, o);
         tmem_wait_ld();
         if (!live) continue;
-        __half hv[32];
+        float v[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) hv[i] = __float2half_rn(__uint_as_float(o[i]) * inv);
-        const long long e0 = base + c4 * 32;
-        if (a.out_dt == F16) {
-            __half* dst = reinterpret_cast<__half*>(a.out) + e0;
-            if (a.out_vec) {
-#pragma unroll
-                for (int v = 0; v < 4; ++v) reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(hv)[v];
-            } else {
-                for (int i = 0; i < 32; ++i) dst[i] = hv[i];
-            }
-        } else if (a.out_dt == BF16) {
-            __nv_bfloat16 bv[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) bv[i] = __float2bfloat16_rn(__half2float(hv[i]));
-            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) + e0;
-            if (a.out_vec) {
-#pragma unroll
-                for (int v = 0; v < 4; ++v) reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(bv)[v];
-            } else {
-                for (int i = 0; i < 32; ++i) dst[i] = bv[i];
-            }
-        } else {
-            float fv[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) fv[i] = __half2float(hv[i]);
-            float* dst = reinterpret_cast<float*>(a.out) + e0;
-            if (a.out_vec) {
-#pragma unroll
-                for (int v = 0; v < 8; ++v) reinterpret_cast<float4*>(dst)[v] = reinterpret_cast<const float4*>(fv)[v];
-            } else {
-                for (int i = 0; i < 32; ++i) dst[i] = fv[i];
-            }
-        }
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(o[i]) * inv;
+        store_out32(a, base + c4 * 32, v);
     }
 }
 

@@ -49,7 +49,7 @@ struct Sage2Cfg {
 // Phase timestamps for kernel development (compiled out unless H3_TRACE is defined): lane 0 of the first warp of
 // each softmax warpgroup and the MMA thread of CTA (0, 0) record clock64() into h3_trace[role][tile][event].
 #ifdef H3_TRACE
-__device__ unsigned long long h3_trace[3][64][8];
+__device__ unsigned long long h3_trace[16][64][8];
 #define H3_T(role, j, ev)                                                                         \
     do {                                                                                          \
         if (blockIdx.x == 0 && blockIdx.y == 0 && (j) < 64) h3_trace[role][j][ev] = clock64();    \

@@ -27,7 +27,7 @@
 #include "../../include/h3sage.h"
 #include "attn.cuh"
 #include "prepass.cuh"
-#include "attn2.cuh"
+#include "attn3.cuh"
 
 namespace {
 
@@ -788,7 +788,7 @@ int h3s_attention_sage_static(void* stream, const void* q, const void* k, const 
     a.v_order = 1;
     a.err = err;
     a.wait_ns = wait_ns;
-    if ((e = launch_sage2(mq, mk, mv, a, st)) != cudaSuccess) return cuda_fail("h3s_attention_sage_static", e);
+    if ((e = launch_sage(mq, mk, mv, a, st)) != cudaSuccess) return cuda_fail("h3s_attention_sage_static", e);
     return 0;
 }
 

@@ -1,5 +1,5 @@
 // h3sage.cu - libh3sage.so: SageAttention v1 for libh3cuda.so, the plugin interface of the reference's kernels/sage.cpp
-// (maxfridbe/sycl_minimax_h3) on sm_100a. The kernel is attn_sage2 (attn2.cuh): int8 Q.K^T on tcgen05 kind::i8,
+// (maxfridbe/sycl_minimax_h3) on sm_100a. The kernel is attn_sage3 (attn3.cuh): int8 Q.K^T on tcgen05 kind::i8,
 // dequantised with the per-block scales, online softmax, P.V in half on kind::f16, two 128-row query tiles per CTA.
 //
 // The reference's plugin wraps Intel's ARK kernel (kernels/sage.cpp:51-52) and its g_err is a process global
@@ -12,7 +12,7 @@
 #include <string>
 
 #include "../../include/h3sage.h"
-#include "attn2.cuh"
+#include "attn3.cuh"
 
 namespace {
 
@@ -78,7 +78,7 @@ int run(cudaStream_t st, const int8_t* q, const int8_t* k, const void* v, int64_
     a.v_order = v_order;
     a.err = err;
     a.wait_ns = wait_ns ? wait_ns : kDefaultWaitNs;
-    const cudaError_t ce = h3::launch_sage2(mq, mk, mv, a, st);
+    const cudaError_t ce = h3::launch_sage(mq, mk, mv, a, st);
     if (ce != cudaSuccess) return fail(std::string("h3sage: launch: ") + cudaGetErrorString(ce));
     return 0;
 }

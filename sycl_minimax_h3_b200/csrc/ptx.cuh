@@ -44,12 +44,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// One non-blocking probe of the phase.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // A wait with a limit. Every spin in these kernels goes through here: after `limit_ns` of global time, or once another
 // role of the CTA has given up (*abort != 0), it stops waiting and returns false. The caller then records the failure
 // in the kernel's error word and winds the CTA down; nothing spins forever.
 // abort may be NULL: the clean-up waits for copies and MMAs still in flight ignore the other roles' failure.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns, const volatile int* abort) {
-    if (mbar_try_wait(bar, parity)) return true;
+// `spin` non-blocking probes come first: a thread suspended in try_wait takes a few hundred cycles to resume after the
+// phase completes, which matters on the softmax <-> MMA chain, where the waits are short; the long waits (producers)
+// pass 0 and sleep at once.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns, const volatile int* abort,
+                                          int spin = 0) {
+    for (int i = 0; i <= spin; ++i)
+        if (mbar_test(bar, parity)) return true;
     const uint64_t t0 = global_ns();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
@@ -58,6 +76,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
             if (global_ns() - t0 > limit_ns) return false;
         }
     }
+}
+
+// mbar_wait by every lane of the warp, the warp agreeing on the result. (Polling by lane 0 alone while the other lanes
+// wait in a shuffle measured far slower on sm_100a: the parked lanes resume late.)
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns, const volatile int* abort,
+                                          int spin = 0) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, limit_ns, abort, spin));
+}
+
+// Named barriers (ids 1-15; 0 is __syncthreads) between warps of a CTA: `count` threads, a multiple of 32, in total
+// across the bar_arrive and bar_sync calls of one phase. bar_sync waits in hardware (no issue slots) and has no limit,
+// so every warp that takes part must make the same sequence of calls on every path, errors included.
+__device__ __forceinline__ void bar_sync(uint32_t id, uint32_t count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void bar_arrive(uint32_t id, uint32_t count) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 // ---- TMA (tensor loads into shared memory, completion counted on an mbarrier). No multicast, ever. ----------------
