@@ -294,8 +294,13 @@ def main() -> None:
     ms_kernel = k0.elapsed_time(k1) / nk
     mixed_peak = 4.0 / 3.0 * peaks["bf16_tflops"]          # half the ops int8 at 2x the bf16 rate, half fp16
     achieved = ops_per_call(S, h, D) / (ms_kernel / 1e3) / 1e12
+    # DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of one ncu capture of this kernel at
+    # S = 16,384, H = 32: 377.26 MB (268.81 read + 108.45 written); q, k, v and out all scale with S*H, so a launch of
+    # this workload moves that times S*H / (16,384 * 32).
+    traffic = 377.26e6 * (S * h) / (16384 * 32)
     roofline = {"bound": "tensor", "achieved": achieved, "peak": mixed_peak, "unit": "TFLOP/s",
-                "frac": achieved / mixed_peak, "traffic": None,
+                "frac": achieved / mixed_peak, "traffic": traffic,
+                "traffic_basis": "ncu DRAM bytes of one launch at S=16384, H=32, scaled by S*H",
                 "kernel": "attn_sage3 (Sage int8 QK^T + fp16 PV, tcgen05, 2 query tiles per CTA)",
                 "peak_basis": f"4/3 x {peaks['source']} bf16 {peaks['bf16_tflops']} TFLOP/s: int8 QK^T at 2x, fp16 PV at 1x",
                 "ms_per_launch": ms_kernel,
@@ -323,32 +328,70 @@ def main() -> None:
                "with_mean_reread_GBs": (pre_bytes + 2.0 * S * h * D) / (ms_pre / 1e3) / 1e9,
                "peak_hbm_GBs": peaks["hbm_gbs"]}
 
-    # ---- end to end: host buffers through the public call, H2D of the inputs and D2H of the output every step ----
+    # ---- end to end: host buffers through the public call. Every step uploads its inputs from pinned host memory and
+    # reads its output back, as a serving loop would run it: step i+1's upload (one copy stream) and step i-1's
+    # read-back (another) overlap step i's attention, with double-buffered device inputs and outputs. The timed region
+    # runs from before the first upload to after the last read-back. The same loop without overlap (one stream) is
+    # reported beside it.
     ne = min(args.steps, 10)
     host_in = [pool[i % len(pool)].cpu().pin_memory() for i in range(2)]
-    host_out = torch.empty(S, h * D, dtype=torch.float16).pin_memory()
-    dev_in = torch.empty_like(pool[0])
-    for i in range(2):
-        dev_in.copy_(host_in[i], non_blocking=True)
-        call(dev_in)
-        host_out.copy_(out, non_blocking=True)
-    torch.cuda.synchronize()
+    host_out = [torch.empty(S, h * D, dtype=torch.float16).pin_memory() for _ in range(2)]
+    dev_in = [torch.empty_like(pool[0]) for _ in range(2)]
+    dev_out = [torch.empty(S, h * D, dtype=torch.float16, device=dev) for _ in range(2)]
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def attend(qkv, o):
+        q, k, v = ops.Rows.qkv(qkv, h, D)
+        ops.attention(q, k, v, o)
+
+    def e2e_loop(n, pipelined):
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev_in = [torch.cuda.Event() for _ in range(2)]
+        ev_done = [torch.cuda.Event() for _ in range(2)]
+        ev_read = [torch.cuda.Event() for _ in range(2)]
+        t0.record(stream)
+        s_in.wait_stream(stream)
+        s_out.wait_stream(stream)
+        for i in range(n):
+            b = i % 2 if pipelined else 0
+            if pipelined:
+                with torch.cuda.stream(s_in):
+                    if i >= 2:
+                        s_in.wait_event(ev_done[b])          # step i-2's attention has read dev_in[b]
+                    dev_in[b].copy_(host_in[i % 2], non_blocking=True)
+                    ev_in[b].record(s_in)
+                stream.wait_event(ev_in[b])
+                if i >= 2:
+                    stream.wait_event(ev_read[b])            # step i-2's output has been read back
+            else:
+                dev_in[b].copy_(host_in[i % 2], non_blocking=True)
+            attend(dev_in[b], dev_out[b])
+            if pipelined:
+                ev_done[b].record(stream)
+                with torch.cuda.stream(s_out):
+                    s_out.wait_event(ev_done[b])
+                    host_out[b].copy_(dev_out[b], non_blocking=True)
+                    ev_read[b].record(s_out)
+            else:
+                host_out[b].copy_(dev_out[b], non_blocking=True)
+        stream.wait_stream(s_out)
+        t1.record(stream)
+        torch.cuda.synchronize()
+        ctx.wait()
+        return t0.elapsed_time(t1) / n
+
+    e2e_loop(2, True)
+    e2e_loop(1, False)
     barrier()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record(stream)
-    for i in range(ne):
-        dev_in.copy_(host_in[i % 2], non_blocking=True)
-        call(dev_in)
-        host_out.copy_(out, non_blocking=True)
-    t1.record(stream)
-    torch.cuda.synchronize()
-    ctx.wait()
+    ms_e2e = max_over_ranks(e2e_loop(ne, True))
     barrier()
-    ms_e2e = max_over_ranks(t0.elapsed_time(t1)) / ne
+    ms_seq = max_over_ranks(e2e_loop(ne, False))
+    barrier()
     e2e = {"value": ops_per_call(S, H, D) / (ms_e2e / 1e3) / 1e12, "unit": UNIT,
-           "h2d_bytes_per_step": int(dev_in.numel() * 2) * world, "d2h_bytes_per_step": int(out.numel() * 2) * world,
-           "ms_per_step": ms_e2e}
-    del host_in, host_out, dev_in
+           "h2d_bytes_per_step": int(dev_in[0].numel() * 2) * world, "d2h_bytes_per_step": int(dev_out[0].numel() * 2) * world,
+           "ms_per_step": ms_e2e, "pipelined": "upload of step i+1 and read-back of step i-1 overlap step i",
+           "ms_per_step_unpipelined": ms_seq}
+    del host_in, host_out, dev_in, dev_out
 
     extra = {}
     if not args.quick:
