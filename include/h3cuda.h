@@ -87,7 +87,8 @@ int h3s_upload_wait(void* ctx);
 /* out = softmax(q . k^T / sqrt(D)) . v, per head. q, k, v: S token rows of H heads x D features, row s at element
  * s * stride (stride >= H * D; 3 * H * D when they sit inside the qkv linear's output), in type dt; out [S, H * D] in
  * out_dt, rounded through half. S >= H3S_SAGE_MIN_S (8192): SageAttention v1 (int8 q, k with per-64-row scales after
- * k's channel mean is taken out; libh3sage.so beside this library); shorter: fp16 SDPA. D = 128. S, H or D <= 0:
+ * k's channel mean is taken out; libh3sage.so beside this library); shorter: fp16 SDPA. D = 64 or 128 (other head
+ * sizes return -1). S, H or D <= 0:
  * nothing to do, returns 0. No score table is ever written: memory stays O(S * H * D). (kernels/h3sycl.h:190-191) */
 int h3s_attention(void* ctx, const void* q, const void* k, const void* v, int dt, int64_t S, int64_t H, int64_t D,
                   int64_t stride, void* out, int out_dt);
@@ -101,7 +102,7 @@ int h3s_attention_batch(void* ctx, const void* q, const void* k, const void* v, 
 
 /* The Sage pre-pass alone (kernels/h3sycl.cpp:1733-1761 as a callable step, for parity checks and for callers that
  * keep int8 q/k): iq, ik int8 [H, S, D]; sc float [2*H*nb + H*D] = q scales [H, nb], k scales [H, nb], k's channel
- * mean [H*D], nb = ceil(S / 64). Queued on the context's stream. */
+ * mean [H*D], nb = ceil(S / 64). D = 64 or 128. Queued on the context's stream. */
 int h3s_sage_prepass(void* ctx, const void* q, const void* k, int dt, int64_t S, int64_t H, int64_t D, int64_t stride,
                      int8_t* iq, int8_t* ik, float* sc);
 /* The CUDA stream a context queues on (a cudaStream_t), for callers that order their own work with it. */

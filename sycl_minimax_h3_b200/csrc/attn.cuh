@@ -57,6 +57,9 @@ struct AttnArgs {
     int q_order, k_order, v_order;   // 0: map dims (D, S, H, B); 1: map dims (D, H, S, B)
     int* err;                   // device error word
     unsigned long long wait_ns; // limit of every wait
+    int D;                      // head size, 64 or 128: the kernels run 128 wide, and a 64-wide head reads as zeros in
+                                // features 64-127 (TMA fills what lies outside the tensor with zeros), so those
+                                // features of Q.K^T add nothing and those of P.V come out 0 and are not stored
 };
 
 template <bool I8>
@@ -143,13 +146,14 @@ __device__ __forceinline__ void store_out32(const AttnArgs& a, long long e0, con
     }
 }
 
-// The epilogue of one query row: O (fp32, 128 TMEM columns from o_taddr) / l, stored at
+// The epilogue of one query row: O (fp32, the first a.D of 128 TMEM columns from o_taddr) / l, stored at
 // out + b*out_seq + qrow*out_tok + h*out_head. Warp-collective (TMEM loads): every lane calls it; rows past S
 // (live = false) load but do not store.
 __device__ __forceinline__ void store_out_row(const AttnArgs& a, int b, int h, int qrow, uint32_t o_taddr, float inv, bool live) {
     const long long base = (long long) b * a.out_seq + (long long) qrow * a.out_tok + (long long) h * a.out_head;
 #pragma unroll
     for (int c4 = 0; c4 < 4; ++c4) {
+        if (c4 * 32 >= a.D) break;
         uint32_t o[32];
         tmem_ld32(o_taddr + c4 * 32, o);
         tmem_wait_ld();

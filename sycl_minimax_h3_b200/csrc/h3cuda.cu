@@ -246,19 +246,26 @@ int prepass_dt(Ctx& c, const void* q, const void* k, int64_t S, int64_t H, int64
     const dim3 grid((unsigned) nb, (unsigned) H);
     const bool vq = aligned16(q) && (stride * es) % 16 == 0 && (D * es) % 16 == 0;
     const bool vk = aligned16(k) && (stride * es) % 16 == 0 && (D * es) % 16 == 0;
-    if (vq) quant_rows<DT, 128, true><<<grid, kQuantThreads, 0, c.st>>>(q, (int) S, stride, nullptr, iq, qs, (int) nb);
-    else quant_rows<DT, 128, false><<<grid, kQuantThreads, 0, c.st>>>(q, (int) S, stride, nullptr, iq, qs, (int) nb);
-    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("quantise q", e);
+    // one quantiser launch: 64-row blocks x heads, the head size a template argument (64 or 128)
+    auto quant = [&](const void* src, const float* mean, int8_t* dst, float* scales, bool vec) {
+        if (D == 64) {
+            if (vec) quant_rows<DT, 64, true><<<grid, kQuantThreads, 0, c.st>>>(src, (int) S, stride, mean, dst, scales, (int) nb);
+            else quant_rows<DT, 64, false><<<grid, kQuantThreads, 0, c.st>>>(src, (int) S, stride, mean, dst, scales, (int) nb);
+        } else {
+            if (vec) quant_rows<DT, 128, true><<<grid, kQuantThreads, 0, c.st>>>(src, (int) S, stride, mean, dst, scales, (int) nb);
+            else quant_rows<DT, 128, false><<<grid, kQuantThreads, 0, c.st>>>(src, (int) S, stride, mean, dst, scales, (int) nb);
+        }
+        return cudaGetLastError();
+    };
+    if ((e = quant(q, nullptr, iq, qs, vq)) != cudaSuccess) return cuda_fail("quantise q", e);
     if ((e = cudaStreamWaitEvent(c.st, c.ev_join, 0)) != cudaSuccess) return cuda_fail("event", e);
-    if (vk) quant_rows<DT, 128, true><<<grid, kQuantThreads, 0, c.st>>>(k, (int) S, stride, kmean, ik, ks, (int) nb);
-    else quant_rows<DT, 128, false><<<grid, kQuantThreads, 0, c.st>>>(k, (int) S, stride, kmean, ik, ks, (int) nb);
-    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("quantise k", e);
+    if ((e = quant(k, kmean, ik, ks, vk)) != cudaSuccess) return cuda_fail("quantise k", e);
     return 0;
 }
 
 int prepass(Ctx& c, const void* q, const void* k, int dt, int64_t S, int64_t H, int64_t D, int64_t stride, int8_t* iq,
             int8_t* ik, float* sc) {
-    if (D != 128) { g_err = "the Sage pre-pass takes D = 128 (got " + std::to_string(D) + ")"; return -1; }
+    if (D != 64 && D != 128) { g_err = "the Sage pre-pass takes D = 64 or 128 (got " + std::to_string(D) + ")"; return -1; }
     switch (dt) {
         case F16: return prepass_dt<F16>(c, q, k, S, H, D, stride, iq, ik, sc);
         case BF16: return prepass_dt<BF16>(c, q, k, S, H, D, stride, iq, ik, sc);
@@ -294,7 +301,7 @@ __global__ void hsd_to_rows(const __half* src, int S, int H, int D, void* out, i
 // ---- Form 0: SageAttention v1 (kernels/h3sycl.cpp:1704-1777). 1 = not a shape this path takes. ----------------------
 int attention_sage(Ctx& c, const void* q, const void* k, const void* v, int dt, int64_t S, int64_t H, int64_t D,
                    int64_t stride, void* out, int out_dt) {
-    if (D != 128 || S > INT32_MAX / D / H) return 1;
+    if ((D != 64 && D != 128) || S > INT32_MAX / D / H) return 1;   // the plugin's bounds (kernels/sage.cpp:33-35)
     const size_t n = (size_t) S * H * D;
     const int64_t nb = (S + kSageBlock - 1) / kSageBlock;
     int8_t* iq = c.grow(c.sq, c.sq_cap, n);
@@ -344,7 +351,7 @@ int attention_sage(Ctx& c, const void* q, const void* k, const void* v, int dt, 
 // ---- Form 1: fp16 SDPA over B sequences (kernels/h3sycl.cpp:1464-1674) ------------------------------------------------
 int attention_sdpa(Ctx& c, const void* q, const void* k, const void* v, int dt, int64_t B, int64_t S, int64_t H, int64_t D,
                    int64_t stride, void* out, int out_dt) {
-    if (D != 128) { g_err = "attention: head size " + std::to_string(D) + " (128 only on this build)"; return -1; }
+    if (D != 64 && D != 128) { g_err = "attention: head size " + std::to_string(D) + " (64 or 128 on this build)"; return -1; }
     if (S > INT32_MAX / 2 || B * H > 65535) { g_err = "attention: sequence or head count out of range"; return -1; }
     Phases ph(c);
     ph.mark();
@@ -390,6 +397,7 @@ int attention_sdpa(Ctx& c, const void* q, const void* k, const void* v, int dt, 
     a.q_order = a.k_order = a.v_order = order;
     a.err = c.err;
     a.wait_ns = c.wait_ns;
+    a.D = (int) D;
     const cudaError_t ce = launch_attn<false>(mq, mk, mv, a, (int) B, c.st);
     if (ce != cudaSuccess) return cuda_fail("attention launch", ce);
     ph.mark();
@@ -788,6 +796,7 @@ int h3s_attention_sage_static(void* stream, const void* q, const void* k, const 
     a.v_order = 1;
     a.err = err;
     a.wait_ns = wait_ns;
+    a.D = (int) D;
     if ((e = launch_sage(mq, mk, mv, a, st)) != cudaSuccess) return cuda_fail("h3s_attention_sage_static", e);
     return 0;
 }

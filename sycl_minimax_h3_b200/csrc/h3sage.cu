@@ -44,7 +44,7 @@ int* own_word() {
 int run(cudaStream_t st, const int8_t* q, const int8_t* k, const void* v, int64_t v_tok, int64_t v_head, void* out,
         int out_dt, int64_t out_tok, int64_t out_head, const float* qscale, const float* kscale, int block, int64_t S,
         int64_t H, int64_t D, float scale, int* err, uint64_t wait_ns) {
-    if (D != 128) return fail("h3sage: head size " + std::to_string(D) + " (128 only on this build)");
+    if (D != 64 && D != 128) return fail("h3sage: head size " + std::to_string(D) + " (64 or 128)");
     if (block <= 0 || block % 64 != 0) return fail("h3sage: the scale block must be a multiple of 64");
     if (S <= 0 || H <= 0 || S > INT32_MAX / D / H) return fail("h3sage: sequence out of range");
     if (out_dt < 0 || out_dt > 2) return fail("h3sage: unknown output type " + std::to_string(out_dt));
@@ -78,6 +78,7 @@ int run(cudaStream_t st, const int8_t* q, const int8_t* k, const void* v, int64_
     a.v_order = v_order;
     a.err = err;
     a.wait_ns = wait_ns ? wait_ns : kDefaultWaitNs;
+    a.D = (int) D;
     const cudaError_t ce = h3::launch_sage(mq, mk, mv, a, st);
     if (ce != cudaSuccess) return fail(std::string("h3sage: launch: ") + cudaGetErrorString(ce));
     return 0;

@@ -184,7 +184,8 @@ def test_error_behaviour(cuda):
     assert L.h3s_attention(ctx.handle, 0, 0, 0, native.F16, 10, 2, 128, 255, 0, native.F16) == -1
     assert "stride" in native.last_error()
     x = torch.zeros(10, 256, dtype=torch.float16, device=cuda)
-    assert L.h3s_attention(ctx.handle, x.data_ptr(), x.data_ptr(), x.data_ptr(), native.F16, 10, 1, 64, 256,
+    # head sizes other than 64 and 128 (the reference plugin's bounds, kernels/sage.cpp:33)
+    assert L.h3s_attention(ctx.handle, x.data_ptr(), x.data_ptr(), x.data_ptr(), native.F16, 10, 1, 96, 256,
                            x.data_ptr(), native.F16) == -1
     assert "head size" in native.last_error()
     assert L.h3s_attention(ctx.handle, x.data_ptr(), x.data_ptr(), x.data_ptr(), 7, 10, 1, 128, 256, x.data_ptr(),
