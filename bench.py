@@ -423,6 +423,7 @@ def main() -> None:
                 os.environ.pop("H3S_SAGE_MIN_S", None)
                 ops._ctx.clear()
             del qkv2, out2
+        extra["rms_rope"] = rms_rope_leg(dev, pool[0], S, h, D, peaks, max_over_ranks, barrier)
         if world > 1:
             extra["c4_ulysses"] = ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier)
 
@@ -452,6 +453,45 @@ def main() -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def rms_rope_leg(dev, qkv, S, h, D, peaks, max_over_ranks, barrier, rot=96) -> dict:
+    """The step before the attention: h3s_rms_rope on q and on k of one c3 block, in place (dit.rs:347-348). HBM-bound:
+    each call reads and writes its S x h x D values once and reads the token's rotation table. The model's rot_dim is
+    6 x its checkpoint's inverse frequencies (dit.rs:71), which the synthetic setup does not have; 96 stands in."""
+    import torch
+
+    from sycl_minimax_h3_b200 import ops
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(4242)
+    w = (1 + 0.1 * torch.randn(D, generator=g, device=dev)).float()
+    ang = torch.rand(S, rot // 2, generator=g, device=dev) * 6.28
+    cs = torch.stack([torch.cos(ang), torch.sin(ang)], -1).float().contiguous()
+    q, k, _ = ops.Rows.qkv(qkv, h, D)
+
+    def both():
+        ops.rms_rope(q, w, 1e-5, cs, rot)
+        ops.rms_rope(k, w, 1e-5, cs, rot)
+
+    for _ in range(3):
+        both()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 20
+    e0.record(torch.cuda.current_stream())
+    for _ in range(n):
+        both()
+    e1.record(torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    ops.context(dev).wait()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / n
+    nbytes = 2 * (2 * S * h * D * qkv.element_size() + S * rot * 4)      # q and k: read + write, and the table
+    return {"kernel": "rms_rope_staged<f16> (q and k, two launches)", "S": S, "heads": h, "rot_dim": rot,
+            "ms_q_and_k": ms, "algorithmic_GBs": nbytes / (ms / 1e3) / 1e9, "peak_hbm_GBs": peaks["hbm_gbs"],
+            "frac": nbytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}
 
 
 def ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier) -> dict:

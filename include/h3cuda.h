@@ -98,6 +98,18 @@ int h3s_attention(void* ctx, const void* q, const void* k, const void* v, int dt
 int h3s_attention_batch(void* ctx, const void* q, const void* k, const void* v, int dt, int64_t B, int64_t S, int64_t H,
                         int64_t D, int64_t stride, void* out, int out_dt);
 
+/* ---- the step before the attention (kernels/h3sycl.h:165-174) --------------------------------------------------- */
+
+/* Per-head RMS norm, then the rotary position rotation, in place: what the denoiser runs on q and k right before
+ * h3s_attention (engine/h3-core/src/dit.rs:347-348). x holds M token rows of H heads x D features, row m at element
+ * m * stride (stride >= H * D), in type x_dt. Each head's features are normalised, s = sum of x*x in feature order,
+ * inv = rsqrt(s / D + eps) (rounded once), x*inv*weight[i] (weight float [D]); then the pairs (i, rot_dim/2 + i),
+ * i < rot_dim/2, are rotated by the token's angle, a' = a*cos - b*sin, b' = b*cos + a*sin, with (cos, sin) from cs
+ * float [M, rot_dim/2, 2]. Features from rot_dim on are only normalised. rot_dim must be even, at most D, and leave an
+ * even remainder, else -1. M, H or D <= 0: nothing to do, returns 0. Queued on the context's stream; no scratch. */
+int h3s_rms_rope(void* ctx, void* x, int x_dt, int64_t M, int64_t H, int64_t D, int64_t stride, const float* weight,
+                 float eps, const float* cs, int rot_dim);
+
 /* ---- additions without a counterpart in the reference ----------------------------------------------------------- */
 
 /* The Sage pre-pass alone (kernels/h3sycl.cpp:1733-1761 as a callable step, for parity checks and for callers that

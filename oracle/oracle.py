@@ -49,6 +49,8 @@ def lib() -> ctypes.CDLL:
         L.orc_exact_rows.argtypes = [P, P, P, I, I64, I64, I64, I64, P, P, I64, P]
         L.orc_attention.argtypes = [P, P, P, I, I64, I64, I64, I64, P, I, I64]
         L.orc_attention.restype = I
+        L.orc_rms_rope.argtypes = [P, I, I64, I64, I64, I64, P, ctypes.c_float, P, I]
+        L.orc_rms_rope.restype = I
         _lib = L
     return _lib
 
@@ -195,3 +197,16 @@ def row_cosines(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     num = np.sum(a * b, axis=1)
     den = np.maximum(np.linalg.norm(a, axis=1) * np.linalg.norm(b, axis=1), 1e-300)
     return num / den
+
+
+def rms_rope(x: np.ndarray, dt: int, M: int, H: int, D: int, stride: int, weight: np.ndarray, eps: float,
+             cs: np.ndarray, rot_dim: int) -> np.ndarray:
+    """Per-head RMS norm + rotary rotation (kernels/h3sycl.cpp:1276-1376) on a copy of x; returns the copy. x holds the
+    element bits (uint16 for half/bfloat16, float32 for float) of M rows at element stride `stride`."""
+    y = np.array(x, copy=True)
+    w = np.ascontiguousarray(weight, np.float32)
+    c = np.ascontiguousarray(cs, np.float32)
+    rc = lib().orc_rms_rope(_p(y), dt, M, H, D, stride, _p(w), ctypes.c_float(eps), _p(c), rot_dim)
+    if rc != 0:
+        raise ValueError("rms_rope: rot_dim must be even, at most D, leave an even remainder; stride >= H*D")
+    return y

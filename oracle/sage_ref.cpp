@@ -16,6 +16,10 @@
 //   fp16 fused SDPA    kernels/h3sycl.cpp:1464-1500 MatMul -> f32 scores, x f32 scale, SoftMax -> f16 P,
 //                                                   MatMul(P, v) -> f16   (oneDNN 3.12 graph, un-vendored)
 //   dispatcher         kernels/h3sycl.cpp:1779-1798 Sage when S >= sage_min_s (8192) and D in {64, 128}, else SDPA
+//   RMS norm + RoPE    kernels/h3sycl.cpp:1276-1376 per (token, head): s = sum of v*v in feature order,
+//                                                   inv = rsqrt(s/D + eps) (correctly rounded here), pairs
+//                                                   (i, rot/2 + i) scaled (x*inv)*w then rotated by (cos, sin),
+//                                                   the rest scaled; rounded back to the element type in place
 //
 // Parity status: the dtype helpers are pinned to the reference's own known-answer tests (engine/h3-core/src/dtype.rs
 // :137-155). The quantiser and the attention arithmetic are UNPINNED: the reference has no test or fixture for them
@@ -362,6 +366,50 @@ int orc_attention(const void* q, const void* k, const void* v, int dt, int64_t S
         for (int64_t h = 0; h < H; ++h)
             for (int64_t d = 0; d < D; ++d)
                 store(out, out_dt, (size_t) ((s * H + h) * D + d), f16_to_f32(ao[(size_t) ((h * S + s) * D + d)]));
+    return 0;
+}
+
+// ---- per-head RMS norm + rotary rotation, in place (kernels/h3sycl.cpp:1276-1376; kernels/h3sycl.h:165-174) -------
+// x: M token rows of H heads x D features at element stride `stride`, type dt; weight [D]; cs [M, rot_dim/2, 2].
+// Returns 0, or -1 for the reference's refusals (rot_dim odd, above D, or leaving an odd remainder; stride < H*D).
+// rsqrt is correctly rounded (the reference's sycl::rsqrt has implementation-defined accuracy).
+int orc_rms_rope(void* x, int dt, int64_t M, int64_t H, int64_t D, int64_t stride, const float* weight, float eps,
+                 const float* cs, int rot_dim) {
+    if (M <= 0 || H <= 0 || D <= 0) return 0;
+    if (rot_dim < 0 || rot_dim > D || rot_dim % 2 != 0 || (D - rot_dim) % 2 != 0) return -1;
+    if (stride < H * D) return -1;
+    const int64_t half = rot_dim / 2;
+    par_for(M * H, 256, [&](int64_t mh, int) {
+        const int64_t m = mh / H, h = mh % H;
+        const size_t base = (size_t) (m * stride + h * D);
+        float s = 0.0f;
+        for (int64_t i = 0; i < D; ++i) {
+            const float v = load(x, dt, base + (size_t) i);
+            s += v * v;
+        }
+        const float arg = s / (float) D + eps;
+        // 1/sqrt(arg) rounded once to float: the double result is within an ulp; the midpoints to its float
+        // neighbours decide (r > mid  <=>  mid^2 * arg < 1, in long double, exact to far below any float tie)
+        float y = (float) (1.0 / std::sqrt((double) arg));
+        if (std::isfinite(y) && y > 0.0f && arg > 0.0f) {
+            const float up = std::nextafter(y, INFINITY), dn = std::nextafter(y, 0.0f);
+            const long double mu = ((long double) y + up) / 2, md = ((long double) y + dn) / 2;
+            if (mu * mu * arg < 1.0L) y = up;
+            else if (md * md * arg > 1.0L) y = dn;
+        }
+        const float inv = y;
+        for (int64_t j = 0; j < half; ++j) {
+            const size_t ia = base + (size_t) j, ib = base + (size_t) (half + j);
+            const float a = load(x, dt, ia) * inv * weight[j];
+            const float b = load(x, dt, ib) * inv * weight[half + j];
+            const size_t t = (size_t) (m * half + j);
+            const float co = cs[2 * t], si = cs[2 * t + 1];
+            store(x, dt, ia, a * co - b * si);
+            store(x, dt, ib, b * co + a * si);
+        }
+        for (int64_t i = rot_dim; i < D; ++i)
+            store(x, dt, base + (size_t) i, load(x, dt, base + (size_t) i) * inv * weight[i]);
+    });
     return 0;
 }
 

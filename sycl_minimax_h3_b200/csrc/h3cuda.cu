@@ -28,6 +28,7 @@
 #include "attn.cuh"
 #include "prepass.cuh"
 #include "attn3.cuh"
+#include "rmsrope.cuh"
 
 namespace {
 
@@ -691,6 +692,28 @@ int h3s_attention_batch(void* ctx, const void* q, const void* k, const void* v, 
         if (rc != 0) return rc;
     }
     return 0;
+}
+
+// kernels/h3sycl.cpp:1276-1376: the reference's refusals and degenerate sizes, the arithmetic in rmsrope.cuh
+int h3s_rms_rope(void* ctx, void* x, int x_dt, int64_t M, int64_t H, int64_t D, int64_t stride, const float* weight,
+                 float eps, const float* cs, int rot_dim) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    if (M <= 0 || H <= 0 || D <= 0) return 0;
+    if (rot_dim < 0 || rot_dim > D || rot_dim % 2 != 0 || (D - rot_dim) % 2 != 0) {
+        g_err = "h3s_rms_rope: rot_dim must be even, at most D, and leave an even remainder";
+        return -1;
+    }
+    if (stride < H * D) { g_err = "h3s_rms_rope: the row stride is shorter than a row"; return -1; }
+    if (!check_dt(x_dt)) { g_err = "h3s_rms_rope: unknown element type " + std::to_string(x_dt); return -1; }
+    if (M * H > (int64_t) INT32_MAX * kRopeRows) { g_err = "h3s_rms_rope: too many rows"; return -1; }
+    DeviceGuard g(c.device);
+    cudaError_t e;
+    switch (x_dt) {
+        case F16: e = launch_rms_rope<F16>(x, M, (int) H, (int) D, stride, weight, eps, cs, rot_dim, c.st); break;
+        case BF16: e = launch_rms_rope<BF16>(x, M, (int) H, (int) D, stride, weight, eps, cs, rot_dim, c.st); break;
+        default: e = launch_rms_rope<F32>(x, M, (int) H, (int) D, stride, weight, eps, cs, rot_dim, c.st); break;
+    }
+    return e == cudaSuccess ? 0 : cuda_fail("h3s_rms_rope", e);
 }
 
 int h3s_sage_prepass(void* ctx, const void* q, const void* k, int dt, int64_t S, int64_t H, int64_t D, int64_t stride,

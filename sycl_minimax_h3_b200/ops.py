@@ -65,6 +65,22 @@ class Rows:
         return Rows(x, 0, heads * dim, x.shape[0], heads, dim)
 
 
+def _floats(t: torch.Tensor, what: str, n: int) -> int:
+    """A float32 device tensor of exactly n values (ops.rs `floats`)."""
+    if t.dtype != torch.float32 or t.numel() != n or not t.is_contiguous():
+        raise H3Error(f"{what}: {n} contiguous float32 values expected, got {list(t.shape)} {t.dtype}")
+    return t.data_ptr()
+
+
+def rms_rope(x: Rows, weight: torch.Tensor, eps: float, cs: torch.Tensor, rot_dim: int) -> None:
+    """Per-head RMS norm (weight float32 [dim]) and the rotary rotation, in place; ``cs`` float32
+    [tokens, rot_dim/2, 2] of (cos, sin) (ops.rs:326-345, kernels/h3sycl.h:165-174)."""
+    ctx = context(x.t.device)
+    ctx.rms_rope(x.ptr(), dt_code(x.t.dtype), x.tokens, x.heads, x.dim, x.stride,
+                 _floats(weight, "the norm weight", x.dim), eps, _floats(cs, "the rotation table", x.tokens * rot_dim),
+                 rot_dim)
+
+
 def attention(q: Rows, k: Rows, v: Rows, out: torch.Tensor) -> None:
     """``out = softmax(q . k^T / sqrt(dim)) . v`` per head; out [tokens, heads * dim] (ops.rs:436-461)."""
     if q.layout() != k.layout() or q.layout() != v.layout():

@@ -200,3 +200,57 @@ def test_golden_fixture(orc, path):
     got = make_golden.compute(orc, f)
     for key, want in got.items():
         assert np.array_equal(np.asarray(f[key]).view(np.uint8), np.asarray(want).view(np.uint8)), f"{path}: {key} differs"
+
+
+# ---- RMS norm + RoPE (kernels/h3sycl.cpp:1276-1376) against an independent numpy restatement -------------------------
+def numpy_rms_rope(x: np.ndarray, M: int, H: int, D: int, w: np.ndarray, eps: float, cs: np.ndarray, rot: int,
+                   narrow) -> np.ndarray:
+    """float32 [M, H, D] values -> results rounded by `narrow`; the same operation order, float32 throughout."""
+    v = x.astype(np.float32)
+    s = np.add.accumulate(v * v, axis=-1, dtype=np.float32)[..., -1]          # feature order, every step rounded
+    arg = (s / np.float32(D) + np.float32(eps)).astype(np.float32)
+    inv = (1.0 / np.sqrt(arg.astype(np.float64))).astype(np.float32)[..., None]
+    half = rot // 2
+    y = (v * inv * w).astype(np.float32)
+    a, b = y[..., :half].copy(), y[..., half:rot].copy()
+    co, si = cs[:, None, :, 0], cs[:, None, :, 1]
+    y[..., :half] = a * co - b * si
+    y[..., half:rot] = b * co + a * si
+    return narrow(y)
+
+
+@pytest.mark.parametrize("D,rot", [(128, 128), (128, 96), (128, 0), (64, 64), (96, 30)])
+@pytest.mark.parametrize("dt", ["f16", "bf16", "f32"])
+def test_rms_rope_matches_numpy(orc, D, rot, dt):
+    rng = np.random.default_rng(D + rot)
+    M, H = 37, 3
+    stride = 3 * H * D
+    vals = (rng.standard_normal((M, stride)) * 3).astype(np.float32)
+    w = (1 + 0.2 * rng.standard_normal(D)).astype(np.float32)
+    ang = rng.uniform(-7, 7, (M, rot // 2)).astype(np.float32)
+    cs = np.ascontiguousarray(np.stack([np.cos(ang), np.sin(ang)], -1).astype(np.float32))
+    if dt == "f16":
+        code, x = orc.F16, vals.astype(np.float16).view(np.uint16)
+        widen, narrow = (lambda b: b.view(np.float16).astype(np.float32)), (lambda y: y.astype(np.float16).view(np.uint16))
+    elif dt == "bf16":
+        code, x = orc.BF16, orc.f32_to_bf16(vals)
+        widen, narrow = orc.bf16_to_f32, (lambda y: orc.f32_to_bf16(np.ascontiguousarray(y)).reshape(y.shape))
+    else:
+        code, x = orc.F32, vals
+        widen, narrow = (lambda b: b), (lambda y: y)
+    got = orc.rms_rope(x, code, M, H, D, stride, w, 1e-5, cs, rot)
+    part = widen(np.ascontiguousarray(x[:, :H * D]).reshape(-1)).reshape(M, H, D)
+    want = numpy_rms_rope(part, M, H, D, w, 1e-5, cs, rot, narrow)
+    assert np.array_equal(np.asarray(got[:, :H * D]).reshape(M, H, D), np.asarray(want).reshape(M, H, D))
+    assert np.array_equal(got[:, H * D:], x[:, H * D:])          # the rest of each row untouched
+
+
+def test_rms_rope_refusals(orc):
+    x = np.zeros((2, 128), np.float32)
+    w = np.ones(128, np.float32)
+    cs = np.zeros(2 * 128, np.float32)
+    for rot in (3, 130, -2):
+        with pytest.raises(ValueError):
+            orc.rms_rope(x, orc.F32, 2, 1, 128, 128, w, 1e-5, cs, rot)
+    with pytest.raises(ValueError):
+        orc.rms_rope(x, orc.F32, 1, 2, 128, 128, w, 1e-5, cs, 128)     # stride < H * D
