@@ -19,6 +19,7 @@
  *                              h3s_wait reports the failure
  *   H3S_SAGE_KERNEL=2          run the earlier Sage kernel (attn_sage2) instead of attn_sage3, for comparison
  *                              (read once per process; libh3sage.so reads it too)
+ *   H3S_SDPA_KERNEL=1          run the earlier fp16 kernel (attn_fwd) instead of attn_sage3's fp16 form, for comparison
  */
 #ifndef H3CUDA_H
 #define H3CUDA_H

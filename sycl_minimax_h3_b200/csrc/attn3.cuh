@@ -33,12 +33,16 @@
 
 namespace h3 {
 
+// I8: the Sage core (int8 Q, K with per-block scales). !I8: the fp16 SDPA (fp16 Q, K; fp32 scores; one scale) in the
+// same structure, for the sequences below the Sage threshold.
+template <bool I8>
 struct Sage3Cfg {
     static constexpr int NQ = 2;                             // query tiles per CTA
-    static constexpr int TILE_B = 128 * 128;                 // a 128-row int8 Q or K tile: one 128-byte column block
+    static constexpr int CB_BYTES = 128 * 128;               // one column block: 128 rows x 128 bytes, 128-byte swizzle
+    static constexpr int TILE_B = I8 ? CB_BYTES : 2 * CB_BYTES;   // a 128-row Q or K tile (int8: 1 block, fp16: 2)
     static constexpr int V_BYTES = kTileN * kHeadDim * 2;    // 32 KB, two column blocks of 64 features
-    static constexpr int CB_BYTES = 128 * 128;
-    static constexpr int NK = 4, NV = 3;
+    static constexpr int NK = I8 ? 4 : 3, NV = I8 ? 3 : 2;   // (fp16: the 32 KB K tiles leave room for fewer stages)
+    static constexpr int KSTEPS = I8 ? 4 : 8;                // MMAs per 64-key half of Q.K^T (K = 32 int8 / 16 fp16)
     static constexpr int OFF_Q = 0;
     static constexpr int OFF_K = OFF_Q + NQ * TILE_B;
     static constexpr int OFF_V = OFF_K + NK * TILE_B;
@@ -49,7 +53,8 @@ struct Sage3Cfg {
     static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
     static constexpr int SMEM = OFF_MISC + 16 + 1024;
     static constexpr int THREADS = 384;
-    static constexpr uint32_t IDESC_QK = idesc(kFmtS32, kFmtS8, kFmtS8, 0, 0, kTileM, 64);   // one half: N = 64 keys
+    static constexpr uint32_t IDESC_QK = I8 ? idesc(kFmtS32, kFmtS8, kFmtS8, 0, 0, kTileM, 64)   // one half: N = 64 keys
+                                            : idesc(kFmtF32, kFmtF16, kFmtF16, 0, 0, kTileM, 64);
     static constexpr uint32_t IDESC_PV = idesc(kFmtF32, kFmtF16, kFmtF16, 0, 1, kTileM, kHeadDim);
     static_assert(SMEM <= 232448, "shared memory budget of one sm_100 CTA");
 };
@@ -63,21 +68,36 @@ constexpr uint32_t kMaskedRaw = 0xFF800000u - kBias;
 #endif
 constexpr int kSpin = H3_SPIN;
 
-// One half row (64 keys) of raw int32 scores r: keys at or past `valid` get kMaskedRaw, then the bias is added in
-// place; returns the biased max.
+// One half row (64 keys) of scores r: keys at or past `valid` are masked. I8: r holds raw int32 sums; masked keys get
+// kMaskedRaw, then the bias is added in place; returns the biased max. !I8: r holds fp32 scores; masked keys get -inf;
+// returns the max.
+template <bool I8>
 __device__ __forceinline__ float sage3_bias_max(uint32_t (&r)[2][32], int valid) {
     if (valid < 64) {
 #pragma unroll
         for (int c2 = 0; c2 < 2; ++c2)
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-                if (c2 * 32 + i >= valid) r[c2][i] = kMaskedRaw;
+                if (c2 * 32 + i >= valid) r[c2][i] = I8 ? kMaskedRaw : 0xFF800000u;
     }
+    if (I8) {
 #pragma unroll
-    for (int c2 = 0; c2 < 2; ++c2)
+        for (int c2 = 0; c2 < 2; ++c2)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) r[c2][i] += kBias;
+            for (int i = 0; i < 32; ++i) r[c2][i] += kBias;
+    }
     return fmaxf(max32(r[0]), max32(r[1]));
+}
+// The exp argument's offset for running max m (log2 units) and scale c: I8 removes the bias too.
+template <bool I8>
+__device__ __forceinline__ float sage3_offset(float c, float m) {
+    if (m == -INFINITY) return 0.0f;           // still no valid key: every weight is 0, not NaN
+    return I8 ? -fmaf(kBiasF, c, m) : -m;
+}
+template <bool I8>
+__device__ __forceinline__ float sage3_scaled_max(float bm, float c) {
+    if (bm == -INFINITY) return -INFINITY;
+    return I8 ? (bm - kBiasF) * c : bm * c;
 }
 
 // exp2 of one half row's 64 biased scores: p = 2^(r*c + k), rounded to half and packed two per word into pk; returns
@@ -106,10 +126,11 @@ __device__ __forceinline__ float sage3_exp_half(const uint32_t (&r)[2][32], floa
     return s.x + s.y;
 }
 
-__global__ void __launch_bounds__(Sage3Cfg::THREADS, 1)
+template <bool I8>
+__global__ void __launch_bounds__(Sage3Cfg<I8>::THREADS, 1)
     attn_sage3(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
-    using C = Sage3Cfg;
+    using C = Sage3Cfg<I8>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bar = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
@@ -173,7 +194,9 @@ __global__ void __launch_bounds__(Sage3Cfg::THREADS, 1)
                 tma_prefetch_desc(&tmK);
                 mbar_expect_tx(q_full, C::NQ * C::TILE_B);
                 for (int t = 0; t < C::NQ; ++t)
-                    tma_rows(sm + C::OFF_Q + t * C::TILE_B, &tmQ, q_full, a.q_order, 0, q0 + t * kTileM, h, b);
+                    for (int cb = 0; cb < C::TILE_B / C::CB_BYTES; ++cb)
+                        tma_rows(sm + C::OFF_Q + t * C::TILE_B + cb * C::CB_BYTES, &tmQ, q_full, a.q_order, cb * 64,
+                                 q0 + t * kTileM, h, b);
             } else {
                 tma_prefetch_desc(&tmV);
             }
@@ -186,7 +209,9 @@ __global__ void __launch_bounds__(Sage3Cfg::THREADS, 1)
                 if (j >= ns && !mbar_wait(empty + st, ((j / ns) - 1) & 1, a.wait_ns, abort)) { ok = false; break; }
                 if (kq) {
                     mbar_expect_tx(full + st, C::TILE_B);
-                    tma_rows(sm + C::OFF_K + st * C::TILE_B, &tmK, full + st, a.k_order, 0, j * kTileN, h, b);
+                    for (int cb = 0; cb < C::TILE_B / C::CB_BYTES; ++cb)
+                        tma_rows(sm + C::OFF_K + st * C::TILE_B + cb * C::CB_BYTES, &tmK, full + st, a.k_order, cb * 64,
+                                 j * kTileN, h, b);
                 } else {
                     mbar_expect_tx(full + st, C::V_BYTES);
                     for (int cb = 0; cb < 2; ++cb)
@@ -215,9 +240,12 @@ __global__ void __launch_bounds__(Sage3Cfg::THREADS, 1)
             const uint32_t q_base = smem_u32(sm + C::OFF_Q + t * C::TILE_B);
             const uint32_t k_base = smem_u32(sm + C::OFF_K + sk * C::TILE_B + half * 64 * 128);
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-                mma_ss_w<true>(tmem + t * kTileN + half * 64, sdesc(q_base + kk * 32, 16, 1024),
-                               sdesc(k_base + kk * 32, 16, 1024), C::IDESC_QK, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < C::KSTEPS; ++kk) {
+                // 32 bytes of K per MMA; fp16 Q, K span two column blocks of 64 features
+                const uint32_t off = (uint32_t) ((kk / 4) * C::CB_BYTES + (kk % 4) * 32);
+                mma_ss_w<I8>(tmem + t * kTileN + half * 64, sdesc(q_base + off, 16, 1024), sdesc(k_base + off, 16, 1024),
+                             C::IDESC_QK, kk > 0 ? 1u : 0u);
+            }
         };
         // O_t += P_t(j).V_j; V_j has landed, P_t(j) is in TMEM
         auto pv = [&](int j) {
@@ -277,7 +305,7 @@ __global__ void __launch_bounds__(Sage3Cfg::THREADS, 1)
         const uint32_t colS = (uint32_t) (t * kTileN), colO = (uint32_t) (2 * kTileN + t * kHeadDim);
         const int qrow = q0 + t * kTileM + row;
         const int S = a.S;
-        const float cq = a.qs[(size_t) h * a.nb + min(qrow, S - 1) / a.blk] * a.scale_log2;
+        const float cq = I8 ? a.qs[(size_t) h * a.nb + min(qrow, S - 1) / a.blk] * a.scale_log2 : a.scale_log2;
         const float* ksh = a.ks + (size_t) h * a.nb;
         const int kpb = a.blk / 64;      // 64-key groups per scale block (1 for the reference's block of 64)
         float m_run = -INFINITY, l_run = 0.0f;
@@ -285,6 +313,7 @@ __global__ void __launch_bounds__(Sage3Cfg::THREADS, 1)
         const bool tr = lane == 0;
         // the K scales of a tile are loaded one tile ahead
         auto ks_of = [&](int jj, float& lo, float& hi) {
+            if (!I8) { lo = hi = 1.0f; return; }
             const int g = min(jj, n_kv - 1) * 2;
             lo = ksh[min(kpb == 1 ? g : g / kpb, a.nb - 1)];
             hi = ksh[min(kpb == 1 ? g + 1 : (g + 1) / kpb, a.nb - 1)];
@@ -327,13 +356,13 @@ __global__ void __launch_bounds__(Sage3Cfg::THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(hi_free + t);
             if (tr) H3_T(warp - 4, j, 1);
-            const float bm_hi = sage3_bias_max(r, S - kv0 - 64);
-            const float sm_hi = bm_hi == -INFINITY ? -INFINITY : (bm_hi - kBiasF) * c_hi;
+            const float bm_hi = sage3_bias_max<I8>(r, S - kv0 - 64);
+            const float sm_hi = sage3_scaled_max<I8>(bm_hi, c_hi);
             if (sm_hi > m_run + 8.0f) m_run = sm_hi;             // also the first finite max
             const float m_hi = m_run;                             // the max the P_hi weights are taken against
             uint32_t p_hi[32];
             take_turn(turns == 0);
-            float sum_hi = sage3_exp_half(r, c_hi, m_run == -INFINITY ? 0.0f : -fmaf(kBiasF, c_hi, m_run), p_hi);
+            float sum_hi = sage3_exp_half(r, c_hi, sage3_offset<I8>(c_hi, m_run), p_hi);
             give_turn();
             ++turns;
             if (tr) H3_T(warp - 4, j, 2);
@@ -346,8 +375,8 @@ __global__ void __launch_bounds__(Sage3Cfg::THREADS, 1)
             tmem_ld32(t_lane + colS + 32, r[1]);
             tmem_wait_ld();
             if (tr) H3_T(warp - 4, j, 3);
-            const float bm_lo = sage3_bias_max(r, S - kv0);
-            const float sm_lo = bm_lo == -INFINITY ? -INFINITY : (bm_lo - kBiasF) * c_lo;
+            const float bm_lo = sage3_bias_max<I8>(r, S - kv0);
+            const float sm_lo = sage3_scaled_max<I8>(bm_lo, c_lo);
             if (sm_lo > m_run + 8.0f) m_run = sm_lo;
             if (__any_sync(0xffffffffu, m_run != m_hi)) {
                 // rare: the low keys moved the max past the one P_hi was taken against (or P_hi had no finite max)
@@ -363,7 +392,7 @@ __global__ void __launch_bounds__(Sage3Cfg::THREADS, 1)
             }
             uint32_t p_lo[32];
             take_turn(false);
-            const float sum_lo = sage3_exp_half(r, c_lo, m_run == -INFINITY ? 0.0f : -fmaf(kBiasF, c_lo, m_run), p_lo);
+            const float sum_lo = sage3_exp_half(r, c_lo, sage3_offset<I8>(c_lo, m_run), p_lo);
             give_turn();
             ++turns;
             tmem_st16(t_lane + colS, *reinterpret_cast<const uint32_t(*)[16]>(&p_lo[0]));
@@ -421,13 +450,15 @@ __global__ void __launch_bounds__(Sage3Cfg::THREADS, 1)
     }
 }
 
+// grid (query-tile pairs, heads x sequences)
+template <bool I8>
 inline cudaError_t launch_sage3(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, const AttnArgs& a,
-                                cudaStream_t st) {
-    using C = Sage3Cfg;
-    cudaError_t e = cudaFuncSetAttribute(attn_sage3, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+                                int B, cudaStream_t st) {
+    using C = Sage3Cfg<I8>;
+    cudaError_t e = cudaFuncSetAttribute(attn_sage3<I8>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
-    dim3 grid((unsigned) ((a.S + C::NQ * kTileM - 1) / (C::NQ * kTileM)), (unsigned) a.H);
-    attn_sage3<<<grid, C::THREADS, C::SMEM, st>>>(q, k, v, a);
+    dim3 grid((unsigned) ((a.S + C::NQ * kTileM - 1) / (C::NQ * kTileM)), (unsigned) (a.H * B));
+    attn_sage3<I8><<<grid, C::THREADS, C::SMEM, st>>>(q, k, v, a);
     return cudaGetLastError();
 }
 
@@ -439,7 +470,18 @@ inline cudaError_t launch_sage(const CUtensorMap& q, const CUtensorMap& k, const
         const char* e = std::getenv("H3S_SAGE_KERNEL");
         return e && std::atoi(e) == 2 ? 2 : 3;
     }();
-    return which == 2 ? launch_sage2(q, k, v, a, st) : launch_sage3(q, k, v, a, st);
+    return which == 2 ? launch_sage2(q, k, v, a, st) : launch_sage3<true>(q, k, v, a, 1, st);
+}
+
+// The fp16 SDPA behind every entry point: attn_sage3<false>; H3S_SDPA_KERNEL=1 selects the earlier attn_fwd<false>
+// (one query tile per CTA, max before exps), kept for comparison.
+inline cudaError_t launch_sdpa(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, const AttnArgs& a, int B,
+                               cudaStream_t st) {
+    static const int which = [] {
+        const char* e = std::getenv("H3S_SDPA_KERNEL");
+        return e && std::atoi(e) == 1 ? 1 : 3;
+    }();
+    return which == 1 ? launch_attn<false>(q, k, v, a, B, st) : launch_sage3<false>(q, k, v, a, B, st);
 }
 
 }  // namespace h3

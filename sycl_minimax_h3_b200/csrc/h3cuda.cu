@@ -399,7 +399,7 @@ int attention_sdpa(Ctx& c, const void* q, const void* k, const void* v, int dt, 
     a.err = c.err;
     a.wait_ns = c.wait_ns;
     a.D = (int) D;
-    const cudaError_t ce = launch_attn<false>(mq, mk, mv, a, (int) B, c.st);
+    const cudaError_t ce = launch_sdpa(mq, mk, mv, a, (int) B, c.st);
     if (ce != cudaSuccess) return cuda_fail("attention launch", ce);
     ph.mark();
     ph.mark();
