@@ -177,6 +177,8 @@ def main() -> None:
     ap.add_argument("--quick", action="store_true", help="main workload only (no c1/c2/c4 side numbers)")
     ap.add_argument("--S", type=int, default=47232, help="tokens of the main workload (profiling runs use a smaller case)")
     ap.add_argument("--H", type=int, default=32, help="heads of the main workload")
+    ap.add_argument("--only", choices=["c1", "c2", "rms_rope"],
+                    help="run one side leg alone and print its numbers (for profiling that kernel); no bench line")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
@@ -215,6 +217,20 @@ def main() -> None:
     if H % world:
         raise SystemExit(f"{H} heads do not split over {world} GPUs")
     h = H // world
+    if args.only:
+        if args.only == "rms_rope":
+            g = torch.Generator(device=dev)
+            g.manual_seed(1000)
+            qkv = torch.randn(S, 3 * h * D, generator=g, device=dev, dtype=torch.float16)
+            res = rms_rope_leg(dev, qkv, S, h, D, peaks, max_over_ranks, barrier)
+        else:
+            res = side_leg(args.only, dev, h, H, D, max_over_ranks, barrier)
+        if rank == 0:
+            print(json.dumps({"only": args.only, **res}), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     nblocks = 50
     stream = torch.cuda.current_stream()
     ctx = ops.context(dev)
@@ -396,33 +412,8 @@ def main() -> None:
     extra = {}
     if not args.quick:
         # c2: 16,848 tokens, Sage; c1: 2,159 tokens, fp16 SDPA (heads split the same way)
-        for name, S2, sage_path in (("c2", 16848, True), ("c1", 2159, False)):
-            qkv2 = make_qkv(S2, h, D, seed=77, device=dev)
-            out2 = torch.empty(S2, h * D, dtype=torch.float16, device=dev)
-            if not sage_path:
-                os.environ["H3S_SAGE_MIN_S"] = str(1 << 30)
-                ops._ctx.clear()
-            q2, k2, v2 = ops.Rows.qkv(qkv2, h, D)
-            for _ in range(3):
-                ops.attention(q2, k2, v2, out2)
-            torch.cuda.synchronize()
-            barrier()
-            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            nrep = 20
-            a0.record(torch.cuda.current_stream())
-            for _ in range(nrep):
-                ops.attention(q2, k2, v2, out2)
-            a1.record(torch.cuda.current_stream())
-            torch.cuda.synchronize()
-            ops.context(dev).wait()
-            barrier()
-            ms2 = max_over_ranks(a0.elapsed_time(a1)) / nrep
-            extra[name] = {"S": S2, "H": H, "ms_per_call": ms2, "tops": ops_per_call(S2, H, D) / (ms2 / 1e3) / 1e12,
-                           "path": "sage" if sage_path else "fp16 sdpa"}
-            if not sage_path:
-                os.environ.pop("H3S_SAGE_MIN_S", None)
-                ops._ctx.clear()
-            del qkv2, out2
+        for name in ("c2", "c1"):
+            extra[name] = side_leg(name, dev, h, H, D, max_over_ranks, barrier)
         extra["rms_rope"] = rms_rope_leg(dev, pool[0], S, h, D, peaks, max_over_ranks, barrier)
         if world > 1:
             extra["c4_ulysses"] = ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier)
@@ -453,6 +444,46 @@ def main() -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+SIDE = {"c2": (16848, True), "c1": (2159, False)}     # tokens, Sage path (else the fp16 SDPA)
+
+
+def side_leg(name, dev, h, H, D, max_over_ranks, barrier) -> dict:
+    """c2 (16,848 tokens, Sage) or c1 (2,159 tokens, fp16 SDPA) on this rank's heads: 20 timed calls."""
+    import torch
+
+    from sycl_minimax_h3_b200 import ops
+    from sycl_minimax_h3_b200.workloads import make_qkv
+
+    S2, sage_path = SIDE[name]
+    qkv2 = make_qkv(S2, h, D, seed=77, device=dev)
+    out2 = torch.empty(S2, h * D, dtype=torch.float16, device=dev)
+    if not sage_path:
+        os.environ["H3S_SAGE_MIN_S"] = str(1 << 30)
+        ops._ctx.clear()
+    try:
+        q2, k2, v2 = ops.Rows.qkv(qkv2, h, D)
+        for _ in range(3):
+            ops.attention(q2, k2, v2, out2)
+        torch.cuda.synchronize()
+        barrier()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        nrep = 20
+        a0.record(torch.cuda.current_stream())
+        for _ in range(nrep):
+            ops.attention(q2, k2, v2, out2)
+        a1.record(torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        ops.context(dev).wait()
+        barrier()
+        ms2 = max_over_ranks(a0.elapsed_time(a1)) / nrep
+    finally:
+        if not sage_path:
+            os.environ.pop("H3S_SAGE_MIN_S", None)
+            ops._ctx.clear()
+    return {"S": S2, "H": H, "ms_per_call": ms2, "tops": ops_per_call(S2, H, D) / (ms2 / 1e3) / 1e12,
+            "path": "sage" if sage_path else "fp16 sdpa"}
 
 
 def rms_rope_leg(dev, qkv, S, h, D, peaks, max_over_ranks, barrier, rot=96) -> dict:

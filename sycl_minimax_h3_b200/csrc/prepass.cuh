@@ -2,8 +2,8 @@
 //
 //   kmean     kmean[h*D+d] = (((0 + k_0) + k_1) + ... + k_{S-1}) / (float) S: one fp32 chain per channel in token order
 //             (the reference's loop, kernels/h3sycl.cpp:1733-1737). A chain cannot be split without changing its bits,
-//             so the work is shaped around it: a TMA ring streams 64-token x 64-channel tiles of k into shared memory
-//             (96 KB in flight per CTA) while 64 threads run the 64 chains over each tile.
+//             so the work is shaped around it: a TMA ring streams 128-token x 32-channel tiles of k into shared memory
+//             (96 KB in flight per CTA) while 32 threads run the 32 chains over each tile.
 //   quant     per (head, 64-row block): m = max|x - mean|, inv = m > 0 ? 127/m : 0, scale = m/127,
 //             q = clamp(round(x * inv), -127, 127), round half away from zero (kernels/h3sycl.cpp:1738-1761).
 //             One CTA per block; the 64 x D values are read once with 16-byte loads and held in registers between the
@@ -55,10 +55,12 @@ __device__ __forceinline__ void ld16(const void* p, float* out) {
 }
 
 // ---- K mean, TMA ring ----------------------------------------------------------------------------------------------
-constexpr int kMeanCh = 64;          // channels per CTA (one chain per thread)
-constexpr int kMeanRows = 64;        // tokens per tile
+constexpr int kMeanCh = 32;          // channels per CTA (one chain per thread): 128 CTAs at H*D = 4096, so that many
+                                     // SMs stream k at once (each chain is latency-bound, one add after the other)
+constexpr int kMeanRows = 128;       // tokens per tile
 constexpr int kMeanRingBytes = 96 * 1024;
-constexpr int kMeanThreads = 96;     // warp 0: producer; warps 1-2: the 64 chains
+constexpr int kMeanThreads = 32 + kMeanCh;   // warp 0: producer; warp 1: one thread per chain
+static_assert(kMeanCh == 32, "the chains are one warp, which frees a ring stage with one arrival");
 
 template <int DT>
 struct MeanCfg {
@@ -80,7 +82,7 @@ __global__ void __launch_bounds__(kMeanThreads) kmean_tma(const __grid_constant_
     const int c0 = blockIdx.x * kMeanCh;
     const int ntile = (S + kMeanRows - 1) / kMeanRows;
     if (threadIdx.x == 0) {
-        for (int i = 0; i < M::NS; ++i) { mbar_init(full + i, 1); mbar_init(empty + i, kMeanCh); }
+        for (int i = 0; i < M::NS; ++i) { mbar_init(full + i, 1); mbar_init(empty + i, 1); }   // one arrival: the chain warp
         *abort = 0;
         fence_barrier_init();
     }
@@ -109,7 +111,8 @@ __global__ void __launch_bounds__(kMeanThreads) kmean_tma(const __grid_constant_
         bool ok = true;
         for (int t = 0; t < ntile; ++t) {
             const int st = t % M::NS;
-            if (!mbar_wait(full + st, (t / M::NS) & 1, wait_ns, abort)) { ok = false; break; }
+            // the whole warp agrees, so that it leaves the loop together (the __syncwarp below needs every lane)
+            if (!warp_wait(full + st, (t / M::NS) & 1, wait_ns, abort)) { ok = false; break; }
             const uint8_t* tile = sm + st * M::TILE;
             const int rows = min(kMeanRows, S - t * kMeanRows);
             if (rows == kMeanRows) {
@@ -119,7 +122,8 @@ __global__ void __launch_bounds__(kMeanThreads) kmean_tma(const __grid_constant_
             } else {
                 for (int r = 0; r < rows; ++r) sum = __fadd_rn(sum, ld1<DT>(tile, (size_t) (r * kMeanCh + c)));
             }
-            mbar_arrive(empty + st);
+            __syncwarp();
+            if (c == 0) mbar_arrive(empty + st);
         }
         if (!ok) { atomicOr(err, kErrPrepass); *abort = 1; }
         else if (c0 + c < C) kmean[c0 + c] = __fdiv_rn(sum, (float) S);
