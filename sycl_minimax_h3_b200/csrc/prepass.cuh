@@ -6,8 +6,8 @@
 //             (96 KB in flight per CTA) while 32 threads run the 32 chains over each tile.
 //   quant     per (head, 64-row block): m = max|x - mean|, inv = m > 0 ? 127/m : 0, scale = m/127,
 //             q = clamp(round(x * inv), -127, 127), round half away from zero (kernels/h3sycl.cpp:1738-1761).
-//             One CTA per block; the 64 x D values are read once with 16-byte loads and held in registers between the
-//             absmax and the quantisation.
+//             One CTA per block; the 64 x D values are read once with 16-byte loads and held in registers (as the raw
+//             chunks) between the absmax and the quantisation.
 //   to_half   any dt -> half [H, S, D] (kernels/h3sycl.cpp:1762-1764), only where the attention cannot read in place.
 //
 // All arithmetic uses the round-to-nearest intrinsics (__fadd_rn, __fsub_rn, __fmul_rn, __fdiv_rn), which the compiler
@@ -161,24 +161,32 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows(const void* src, int
     float mu[EPC];
 #pragma unroll
     for (int e = 0; e < EPC; ++e) mu[e] = mean ? mean[h * D + col + e] : 0.0f;
-    float x[NCH][EPC];
-    float m = 0.0f;
+    // the raw 16-byte chunks stay in registers between the two passes (half the registers of the converted floats,
+    // so more CTAs, and more loads in flight, per SM); each pass converts them the same way
+    uint4 raw[NCH];
 #pragma unroll
     for (int i = 0; i < NCH; ++i) {
         const int r = rsub + i * RSTEP;
+        raw[i] = make_uint4(0, 0, 0, 0);
         if (r < rows) {
             const size_t base = (size_t) (r0 + r) * (size_t) stride + (size_t) (h * D + col);
             if constexpr (VEC) {
-                ld16<DT>(reinterpret_cast<const uint8_t*>(src) + base * DtInfo<DT>::ES, x[i]);
+                raw[i] = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(src) + base * DtInfo<DT>::ES);
             } else {
+                uint8_t* rb = reinterpret_cast<uint8_t*>(&raw[i]);
 #pragma unroll
-                for (int e = 0; e < EPC; ++e) x[i][e] = ld1<DT>(src, base + e);
+                for (int e = 0; e < 16; ++e) rb[e] = reinterpret_cast<const uint8_t*>(src)[base * DtInfo<DT>::ES + e];
             }
+        }
+    }
+    float m = 0.0f;
 #pragma unroll
-            for (int e = 0; e < EPC; ++e) {
-                x[i][e] = __fsub_rn(x[i][e], mu[e]);
-                m = fmaxf(m, fabsf(x[i][e]));
-            }
+    for (int i = 0; i < NCH; ++i) {
+        if (rsub + i * RSTEP < rows) {
+            float x[EPC];
+            ld16<DT>(&raw[i], x);
+#pragma unroll
+            for (int e = 0; e < EPC; ++e) m = fmaxf(m, fabsf(__fsub_rn(x[e], mu[e])));
         }
     }
     // block absmax
@@ -196,9 +204,12 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows(const void* src, int
     for (int i = 0; i < NCH; ++i) {
         const int r = rsub + i * RSTEP;
         if (r < rows) {
+            float x[EPC];
+            ld16<DT>(&raw[i], x);
             int8_t qv[EPC];
 #pragma unroll
-            for (int e = 0; e < EPC; ++e) qv[e] = (int8_t) fminf(127.0f, fmaxf(-127.0f, roundf(__fmul_rn(x[i][e], inv))));
+            for (int e = 0; e < EPC; ++e)
+                qv[e] = (int8_t) fminf(127.0f, fmaxf(-127.0f, roundf(__fmul_rn(__fsub_rn(x[e], mu[e]), inv))));
             int8_t* d = dst + ((size_t) h * S + r0 + r) * D + col;
             if constexpr (EPC == 8) *reinterpret_cast<uint2*>(d) = *reinterpret_cast<const uint2*>(qv);
             else *reinterpret_cast<uint32_t*>(d) = *reinterpret_cast<const uint32_t*>(qv);
