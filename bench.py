@@ -177,7 +177,7 @@ def main() -> None:
     ap.add_argument("--quick", action="store_true", help="main workload only (no c1/c2/c4 side numbers)")
     ap.add_argument("--S", type=int, default=47232, help="tokens of the main workload (profiling runs use a smaller case)")
     ap.add_argument("--H", type=int, default=32, help="heads of the main workload")
-    ap.add_argument("--only", choices=["c1", "c2", "rms_rope"],
+    ap.add_argument("--only", choices=["c1", "c2", "rms_rope", "causal"],
                     help="run one side leg alone and print its numbers (for profiling that kernel); no bench line")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -218,7 +218,9 @@ def main() -> None:
         raise SystemExit(f"{H} heads do not split over {world} GPUs")
     h = H // world
     if args.only:
-        if args.only == "rms_rope":
+        if args.only == "causal":
+            res = causal_leg(dev, max_over_ranks, barrier)
+        elif args.only == "rms_rope":
             g = torch.Generator(device=dev)
             g.manual_seed(1000)
             qkv = torch.randn(S, 3 * h * D, generator=g, device=dev, dtype=torch.float16)
@@ -415,6 +417,7 @@ def main() -> None:
         for name in ("c2", "c1"):
             extra[name] = side_leg(name, dev, h, H, D, max_over_ranks, barrier)
         extra["rms_rope"] = rms_rope_leg(dev, pool[0], S, h, D, peaks, max_over_ranks, barrier)
+        extra["causal"] = causal_leg(dev, max_over_ranks, barrier)
         if world > 1:
             extra["c4_ulysses"] = ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier)
 
@@ -523,6 +526,40 @@ def rms_rope_leg(dev, qkv, S, h, D, peaks, max_over_ranks, barrier, rot=96) -> d
     return {"kernel": "rms_rope_staged<f16> (q and k, two launches)", "S": S, "heads": h, "rot_dim": rot,
             "ms_q_and_k": ms, "algorithmic_GBs": nbytes / (ms / 1e3) / 1e9, "peak_hbm_GBs": peaks["hbm_gbs"],
             "frac": nbytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}
+
+
+def causal_leg(dev, max_over_ranks, barrier, L=512, Hq=32, Hkv=8, D=128) -> dict:
+    """The text encoder's causal attention with grouped heads (h3s_attention_causal, te.rs:340-346) on one prompt: fp16,
+    q [L, Hq*D], k and v [L, Hkv*D], seeded normal values. The encoder's head counts come from its checkpoint, which
+    the synthetic setup does not have; 32 query over 8 key/value heads of 128 stand in. Work: 4*D*Hq*L*(L+1)/2 flops."""
+    import torch
+
+    from sycl_minimax_h3_b200 import ops
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(77)
+    q = torch.randn(L, Hq * D, generator=g, device=dev, dtype=torch.float16)
+    k = torch.randn(L, Hkv * D, generator=g, device=dev, dtype=torch.float16)
+    v = torch.randn(L, Hkv * D, generator=g, device=dev, dtype=torch.float16)
+    out = torch.empty(L, Hq * D, device=dev, dtype=torch.float16)
+    rq, rk, rv = ops.Rows.packed(q, Hq, D), ops.Rows.packed(k, Hkv, D), ops.Rows.packed(v, Hkv, D)
+    for _ in range(3):
+        ops.attention_causal(rq, rk, rv, out)
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 20
+    e0.record(torch.cuda.current_stream())
+    for _ in range(n):
+        ops.attention_causal(rq, rk, rv, out)
+    e1.record(torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    ops.context(dev).wait()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / n
+    flops = 4.0 * D * Hq * L * (L + 1) / 2
+    return {"kernel": "attn_causal<f16> (CUDA cores, fp32 weights)", "L": L, "Hq": Hq, "Hkv": Hkv, "D": D, "ms": ms,
+            "tflops": flops / (ms / 1e3) / 1e12}
 
 
 def ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier) -> dict:

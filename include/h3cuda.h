@@ -111,6 +111,16 @@ int h3s_attention_batch(void* ctx, const void* q, const void* k, const void* v, 
 int h3s_rms_rope(void* ctx, void* x, int x_dt, int64_t M, int64_t H, int64_t D, int64_t stride, const float* weight,
                  float eps, const float* cs, int rot_dim);
 
+/* ---- the text encoder's attention (kernels/h3sycl.h:105-108) ---------------------------------------------------- */
+
+/* Causal attention with grouped heads, for short sequences (the text encoder, engine/h3-core/src/te.rs:340-346): Hq
+ * query heads share Hkv key/value heads (query head h reads key/value head h / (Hq / Hkv)). q rows of stride qs, k and
+ * v rows of stride kvs (elements), type dt; out [L, Hq * D] in dt. Query i attends to keys 0..i with scores
+ * q.k / sqrt(D), and every weight stays fp32 (nothing is rounded to half between the loads and the store).
+ * D <= 256 and Hq a multiple of Hkv, else -1; L <= 0: nothing to do, returns 0. Queued on the context's stream. */
+int h3s_attention_causal(void* ctx, const void* q, const void* k, const void* v, int dt, int64_t L, int64_t Hq,
+                         int64_t Hkv, int64_t D, int64_t qs, int64_t kvs, void* out);
+
 /* ---- additions without a counterpart in the reference ----------------------------------------------------------- */
 
 /* The Sage pre-pass alone (kernels/h3sycl.cpp:1733-1761 as a callable step, for parity checks and for callers that

@@ -51,6 +51,8 @@ def lib() -> ctypes.CDLL:
         L.orc_attention.restype = I
         L.orc_rms_rope.argtypes = [P, I, I64, I64, I64, I64, P, ctypes.c_float, P, I]
         L.orc_rms_rope.restype = I
+        L.orc_attention_causal.argtypes = [P, P, P, I, I64, I64, I64, I64, I64, I64, P]
+        L.orc_attention_causal.restype = I
         _lib = L
     return _lib
 
@@ -210,3 +212,14 @@ def rms_rope(x: np.ndarray, dt: int, M: int, H: int, D: int, stride: int, weight
     if rc != 0:
         raise ValueError("rms_rope: rot_dim must be even, at most D, leave an even remainder; stride >= H*D")
     return y
+
+
+def attention_causal(q, k, v, dt: int, L: int, Hq: int, Hkv: int, D: int, qs: int, kvs: int) -> np.ndarray:
+    """Causal attention with grouped heads (kernels/h3sycl.cpp:870-898): q rows of stride qs, k and v rows of stride kvs
+    (element bits of type dt; each argument may be an (array, element offset) pair); returns out [L, Hq*D] in dt bits."""
+    base = q[0] if isinstance(q, tuple) else q
+    out = np.zeros((L, Hq * D), dtype=base.dtype)
+    rc = lib().orc_attention_causal(_p(q), _p(k), _p(v), dt, L, Hq, Hkv, D, qs, kvs, _p(out))
+    if rc != 0:
+        raise ValueError("attention_causal: D <= 256 and Hq a multiple of Hkv")
+    return out

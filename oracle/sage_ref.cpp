@@ -16,6 +16,8 @@
 //   fp16 fused SDPA    kernels/h3sycl.cpp:1464-1500 MatMul -> f32 scores, x f32 scale, SoftMax -> f16 P,
 //                                                   MatMul(P, v) -> f16   (oneDNN 3.12 graph, un-vendored)
 //   dispatcher         kernels/h3sycl.cpp:1779-1798 Sage when S >= sage_min_s (8192) and D in {64, 128}, else SDPA
+//   causal GQA attn    kernels/h3sycl.cpp:870-898   per (head, query i): online softmax over keys j <= i in fp32,
+//                                                   s = (q.k) * 1/sqrt(D), exp, acc = acc*a + e*v, out = acc / l
 //   RMS norm + RoPE    kernels/h3sycl.cpp:1276-1376 per (token, head): s = sum of v*v in feature order,
 //                                                   inv = rsqrt(s/D + eps) (correctly rounded here), pairs
 //                                                   (i, rot/2 + i) scaled (x*inv)*w then rotated by (cos, sin),
@@ -409,6 +411,37 @@ int orc_rms_rope(void* x, int dt, int64_t M, int64_t H, int64_t D, int64_t strid
         }
         for (int64_t i = rot_dim; i < D; ++i)
             store(x, dt, base + (size_t) i, load(x, dt, base + (size_t) i) * inv * weight[i]);
+    });
+    return 0;
+}
+
+// ---- causal attention with grouped heads (kernels/h3sycl.cpp:870-898; kernels/h3sycl.h:105-108) --------------------
+// q rows of stride qs, k and v rows of stride kvs (elements), type dt; out [L, Hq*D] in dt. Query head h reads
+// key/value head h / (Hq/Hkv). Every value is fp32 between the loads and the store (the reference never rounds P).
+// The dot product is summed in feature order here (the reference's work-group reduction leaves its order open).
+// Returns 0, or -1 for the reference's refusals (D > 256, Hq not a multiple of Hkv).
+int orc_attention_causal(const void* q, const void* k, const void* v, int dt, int64_t L, int64_t Hq, int64_t Hkv,
+                         int64_t D, int64_t qs, int64_t kvs, void* out) {
+    if (L <= 0) return 0;
+    if (D > 256 || Hkv <= 0 || Hq % Hkv != 0) return -1;
+    const float scale = 1.0f / std::sqrt((float) D);
+    par_for(Hq * L, 16, [&](int64_t hi, int) {
+        const int64_t h = hi / L, i = hi % L, g = h / (Hq / Hkv);
+        float m = -INFINITY, l = 0.0f;
+        std::vector<float> acc((size_t) D, 0.0f);
+        for (int64_t j = 0; j <= i; ++j) {
+            float dot = 0.0f;
+            for (int64_t d = 0; d < D; ++d)
+                dot += load(q, dt, (size_t) (i * qs + h * D + d)) * load(k, dt, (size_t) (j * kvs + g * D + d));
+            const float sc = dot * scale;
+            const float mn = std::fmax(m, sc);
+            const float a = std::exp(m - mn), e = std::exp(sc - mn);
+            for (int64_t d = 0; d < D; ++d)
+                acc[(size_t) d] = acc[(size_t) d] * a + e * load(v, dt, (size_t) (j * kvs + g * D + d));
+            l = l * a + e;
+            m = mn;
+        }
+        for (int64_t d = 0; d < D; ++d) store(out, dt, (size_t) (i * Hq * D + h * D + d), acc[(size_t) d] / l);
     });
     return 0;
 }

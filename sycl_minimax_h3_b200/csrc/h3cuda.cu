@@ -29,6 +29,7 @@
 #include "prepass.cuh"
 #include "attn3.cuh"
 #include "rmsrope.cuh"
+#include "causal.cuh"
 
 namespace {
 
@@ -692,6 +693,28 @@ int h3s_attention_batch(void* ctx, const void* q, const void* k, const void* v, 
         if (rc != 0) return rc;
     }
     return 0;
+}
+
+// kernels/h3sycl.cpp:870-898: the reference's refusals (D <= 256, Hq a multiple of Hkv), the arithmetic in causal.cuh
+int h3s_attention_causal(void* ctx, const void* q, const void* k, const void* v, int dt, int64_t L, int64_t Hq,
+                         int64_t Hkv, int64_t D, int64_t qs, int64_t kvs, void* out) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    if (L <= 0) return 0;
+    if (D <= 0 || D > 256 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0) {
+        g_err = "h3s_attention_causal: D <= 256, Hq a multiple of Hkv";
+        return -1;
+    }
+    if (qs < Hq * D || kvs < Hkv * D) { g_err = "h3s_attention_causal: a row stride is shorter than its heads"; return -1; }
+    if (!check_dt(dt)) { g_err = "h3s_attention_causal: unknown element type " + std::to_string(dt); return -1; }
+    if (L > INT32_MAX / Hq) { g_err = "h3s_attention_causal: too many rows"; return -1; }
+    DeviceGuard g(c.device);
+    cudaError_t e;
+    switch (dt) {
+        case F16: e = launch_causal<F16>(q, k, v, (int) L, (int) Hq, (int) Hkv, (int) D, qs, kvs, out, c.st); break;
+        case BF16: e = launch_causal<BF16>(q, k, v, (int) L, (int) Hq, (int) Hkv, (int) D, qs, kvs, out, c.st); break;
+        default: e = launch_causal<F32>(q, k, v, (int) L, (int) Hq, (int) Hkv, (int) D, qs, kvs, out, c.st); break;
+    }
+    return e == cudaSuccess ? 0 : cuda_fail("h3s_attention_causal", e);
 }
 
 // kernels/h3sycl.cpp:1276-1376: the reference's refusals and degenerate sizes, the arithmetic in rmsrope.cuh

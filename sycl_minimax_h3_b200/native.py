@@ -43,6 +43,7 @@ CUDA_SYMBOLS = [
     ("h3s_attention", I, [P, P, P, P, I, I64, I64, I64, I64, P, I]),
     ("h3s_attention_batch", I, [P, P, P, P, I, I64, I64, I64, I64, I64, P, I]),
     ("h3s_rms_rope", I, [P, P, I, I64, I64, I64, I64, P, ctypes.c_float, P, I]),
+    ("h3s_attention_causal", I, [P, P, P, P, I, I64, I64, I64, I64, I64, I64, P]),
     ("h3s_sage_prepass", I, [P, P, P, I, I64, I64, I64, I64, P, P, P]),
     ("h3s_stream", P, [P]),
     ("h3s_selftest_wait_timeout", I, [P, U64]),
@@ -197,6 +198,10 @@ class Context:
     def rms_rope(self, x: int, dt: int, M: int, H: int, D: int, stride: int, weight: int, eps: float, cs: int,
                  rot_dim: int) -> None:
         check(self._lib.h3s_rms_rope(self.handle, x, dt, M, H, D, stride, weight, eps, cs, rot_dim), "h3s_rms_rope")
+
+    def attention_causal(self, q: int, k: int, v: int, dt: int, L: int, Hq: int, Hkv: int, D: int, qs: int, kvs: int,
+                         out: int) -> None:
+        check(self._lib.h3s_attention_causal(self.handle, q, k, v, dt, L, Hq, Hkv, D, qs, kvs, out), "h3s_attention_causal")
 
     def sage_prepass(self, q: int, k: int, dt: int, S: int, H: int, D: int, stride: int, iq: int, ik: int, sc: int) -> None:
         check(self._lib.h3s_sage_prepass(self.handle, q, k, dt, S, H, D, stride, iq, ik, sc), "h3s_sage_prepass")

@@ -81,6 +81,23 @@ def rms_rope(x: Rows, weight: torch.Tensor, eps: float, cs: torch.Tensor, rot_di
                  rot_dim)
 
 
+def attention_causal(q: Rows, k: Rows, v: Rows, out: torch.Tensor) -> None:
+    """Causal attention with grouped heads (the text encoder's call, te.rs:340-346): q has the query heads, k and v the
+    key/value heads (a divisor of them), all with the same tokens and head size; out [tokens, q.heads * dim] in q's
+    type (kernels/h3sycl.h:105-108)."""
+    if k.layout()[1:3] != v.layout()[1:3] or k.stride != v.stride or q.tokens != k.tokens or k.tokens != v.tokens:
+        raise H3Error("attention_causal: k and v must have the same layout, and q, k, v the same tokens")
+    if q.dim != k.dim or k.heads == 0 or q.heads % k.heads != 0:
+        raise H3Error(f"attention_causal: {q.heads} query heads over {k.heads} key/value heads of {k.dim}")
+    if q.t.dtype != k.t.dtype or q.t.dtype != v.t.dtype or out.dtype != q.t.dtype:
+        raise H3Error("attention_causal: q, k, v and out must have one element type")
+    if out.numel() != q.tokens * q.heads * q.dim or not out.is_contiguous():
+        raise H3Error(f"attention_causal: out {list(out.shape)} for {q.tokens} tokens of {q.heads} x {q.dim}")
+    ctx = context(out.device)
+    ctx.attention_causal(q.ptr(), k.ptr(), v.ptr(), dt_code(q.t.dtype), q.tokens, q.heads, k.heads, q.dim, q.stride,
+                         k.stride, out.data_ptr())
+
+
 def attention(q: Rows, k: Rows, v: Rows, out: torch.Tensor) -> None:
     """``out = softmax(q . k^T / sqrt(dim)) . v`` per head; out [tokens, heads * dim] (ops.rs:436-461)."""
     if q.layout() != k.layout() or q.layout() != v.layout():

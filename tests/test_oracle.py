@@ -254,3 +254,37 @@ def test_rms_rope_refusals(orc):
             orc.rms_rope(x, orc.F32, 2, 1, 128, 128, w, 1e-5, cs, rot)
     with pytest.raises(ValueError):
         orc.rms_rope(x, orc.F32, 1, 2, 128, 128, w, 1e-5, cs, 128)     # stride < H * D
+
+
+# ---- causal attention with grouped heads (kernels/h3sycl.cpp:870-898) against float64 numpy ---------------------------
+def numpy_causal(q, k, v, L, Hq, Hkv, D):
+    """float64 causal softmax attention; q [L, Hq, D], k, v [L, Hkv, D] as float64."""
+    out = np.zeros((L, Hq, D))
+    grp = Hq // Hkv
+    mask = np.tril(np.ones((L, L), bool))
+    for h in range(Hq):
+        s = q[:, h, :] @ k[:, h // grp, :].T / np.sqrt(D)
+        s = np.where(mask, s, -np.inf)
+        p = np.exp(s - s.max(1, keepdims=True))
+        out[:, h, :] = (p / p.sum(1, keepdims=True)) @ v[:, h // grp, :]
+    return out
+
+
+@pytest.mark.parametrize("L,Hq,Hkv,D", [(1, 2, 1, 128), (37, 4, 2, 128), (90, 3, 3, 64), (50, 4, 1, 96)])
+def test_causal_matches_float64(orc, L, Hq, Hkv, D):
+    rng = np.random.default_rng(L + D)
+    q = rng.standard_normal((L, Hq * D)).astype(np.float32)
+    k = rng.standard_normal((L, Hkv * D)).astype(np.float32)
+    v = rng.standard_normal((L, Hkv * D)).astype(np.float32)
+    got = orc.attention_causal(q, k, v, orc.F32, L, Hq, Hkv, D, Hq * D, Hkv * D)
+    want = numpy_causal(q.reshape(L, Hq, D).astype(np.float64), k.reshape(L, Hkv, D).astype(np.float64),
+                        v.reshape(L, Hkv, D).astype(np.float64), L, Hq, Hkv, D)
+    assert np.max(np.abs(got.reshape(L, Hq, D) - want)) < 1e-5
+
+
+def test_causal_refusals(orc):
+    x = np.zeros((2, 512), np.float32)
+    with pytest.raises(ValueError):
+        orc.attention_causal(x, x, x, orc.F32, 2, 1, 1, 512, 512, 512)      # D > 256
+    with pytest.raises(ValueError):
+        orc.attention_causal(x, x, x, orc.F32, 2, 3, 2, 128, 512, 512)      # Hq not a multiple of Hkv
