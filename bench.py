@@ -177,7 +177,7 @@ def main() -> None:
     ap.add_argument("--quick", action="store_true", help="main workload only (no c1/c2/c4 side numbers)")
     ap.add_argument("--S", type=int, default=47232, help="tokens of the main workload (profiling runs use a smaller case)")
     ap.add_argument("--H", type=int, default=32, help="heads of the main workload")
-    ap.add_argument("--only", choices=["c1", "c2", "rms_rope", "causal"],
+    ap.add_argument("--only", choices=["c1", "c2", "rms_rope", "causal", "int8_linear"],
                     help="run one side leg alone and print its numbers (for profiling that kernel); no bench line")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -220,6 +220,8 @@ def main() -> None:
     if args.only:
         if args.only == "causal":
             res = causal_leg(dev, max_over_ranks, barrier)
+        elif args.only == "int8_linear":
+            res = int8_linear_leg(dev, S, peaks, max_over_ranks, barrier)
         elif args.only == "rms_rope":
             g = torch.Generator(device=dev)
             g.manual_seed(1000)
@@ -418,6 +420,7 @@ def main() -> None:
             extra[name] = side_leg(name, dev, h, H, D, max_over_ranks, barrier)
         extra["rms_rope"] = rms_rope_leg(dev, pool[0], S, h, D, peaks, max_over_ranks, barrier)
         extra["causal"] = causal_leg(dev, max_over_ranks, barrier)
+        extra["int8_linear"] = int8_linear_leg(dev, S, peaks, max_over_ranks, barrier)
         if world > 1:
             extra["c4_ulysses"] = ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier)
 
@@ -560,6 +563,43 @@ def causal_leg(dev, max_over_ranks, barrier, L=512, Hq=32, Hkv=8, D=128) -> dict
     flops = 4.0 * D * Hq * L * (L + 1) / 2
     return {"kernel": "attn_causal<f16> (CUDA cores, fp32 weights)", "L": L, "Hq": Hq, "Hkv": Hkv, "D": D, "ms": ms,
             "tflops": flops / (ms / 1e3) / 1e12}
+
+
+def int8_linear_leg(dev, M, peaks, max_over_ranks, barrier, K=4096, N=12288, group=256) -> dict:
+    """The qkv projection of one denoiser block (h3s_int8_linear, ops.rs:25-80): M tokens x hidden 4096 -> 3 x 4096,
+    int8 weights stored rotated in groups of 256 with one scale per output, no bias, bf16 in and out (dit.rs:130-140).
+    Seeded normal activations and random int8 weights stand in for a checkpoint's. Each call runs rotq_rows (HBM-bound:
+    reads x, writes its int8 copy) and i8gemm (tensor-bound: 2*M*N*K int8 operations); inputs larger than L2."""
+    import torch
+
+    from sycl_minimax_h3_b200 import ops
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(31)
+    x = torch.randn(M, K, generator=g, device=dev).to(torch.bfloat16)
+    w = torch.randint(-127, 128, (N, K), generator=g, device=dev, dtype=torch.int8)
+    ws = (torch.rand(N, generator=g, device=dev) * 0.01 + 1e-3).float()
+    out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    lin = ops.Int8Linear(w, ws, None, group)
+    for _ in range(3):
+        lin.forward(x, out)
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 20
+    e0.record(torch.cuda.current_stream())
+    for _ in range(n):
+        lin.forward(x, out)
+    e1.record(torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    ops.context(dev).wait()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / n
+    tops = 2.0 * M * N * K / (ms / 1e3) / 1e12
+    peak = 2 * peaks["bf16_tflops"]
+    return {"kernels": "rotq_rows<bf16,256> + i8gemm (tcgen05 kind::i8, 128x256 tiles)", "M": M, "K": K, "N": N,
+            "group": group, "ms": ms, "tops": tops, "peak_int8_tops": peak, "peak_source": peaks["source"],
+            "frac": tops / peak}
 
 
 def ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier) -> dict:

@@ -111,6 +111,25 @@ int h3s_attention_batch(void* ctx, const void* q, const void* k, const void* v, 
 int h3s_rms_rope(void* ctx, void* x, int x_dt, int64_t M, int64_t H, int64_t D, int64_t stride, const float* weight,
                  float eps, const float* cs, int rot_dim);
 
+/* ---- the block's linear layers (kernels/h3sycl.h:74-85) ----------------------------------------------------------- */
+
+/* A linear layer with int8 weights and activations quantised on the fly (the int8_convrot checkpoints' layers: qkv,
+ * out_proj, fc1, fc2 of every denoiser block, engine/h3-core/src/ops.rs:25-80):
+ *
+ *   x_rot = x . H           per group of `group` features, H the normalised Hadamard matrix h4 (x) h4 (x) ...
+ *   s_r   = max(max|x_rot[r]| / 127, 1e-30)                  per row
+ *   q     = clamp(rint(x_rot / s_r), -128, 127)              int8
+ *   acc   = q . W^T                                          int32, on the tensor cores
+ *   out   = acc * (s_r * wscale) + bias    (n_wscale = 1)    or   (acc * s_r) * wscale[n] + bias   (n_wscale = N)
+ *
+ * x [M, K] in x_dt; w int8 [N, K]; wscale float32 [n_wscale]; bias float32 [N] or NULL; out [M, N] in out_dt.
+ * group = 0: no rotation; else a power of 2 up to 256 dividing K (as the reference accepts; 4^n is what checkpoints
+ * use), else -1 "unsupported ConvRot group size". n_wscale must be 1 or N. M, K or N <= 0: nothing to do, returns 0.
+ * Queued on the context's stream; the int8 copy of x is context scratch (grow-only, at most 1 GiB: longer inputs
+ * run in row chunks). */
+int h3s_int8_linear(void* ctx, const void* x, int x_dt, int64_t M, int64_t K, const int8_t* w, int64_t N,
+                    const float* wscale, int64_t n_wscale, const float* bias, void* out, int out_dt, int group);
+
 /* ---- the text encoder's attention (kernels/h3sycl.h:105-108) ---------------------------------------------------- */
 
 /* Causal attention with grouped heads, for short sequences (the text encoder, engine/h3-core/src/te.rs:340-346): Hq

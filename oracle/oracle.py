@@ -53,6 +53,9 @@ def lib() -> ctypes.CDLL:
         L.orc_rms_rope.restype = I
         L.orc_attention_causal.argtypes = [P, P, P, I, I64, I64, I64, I64, I64, I64, P]
         L.orc_attention_causal.restype = I
+        L.orc_rotq.argtypes = [P, I, I64, I64, I, P, P]
+        L.orc_int8_linear.argtypes = [P, I, I64, I64, P, I64, P, I64, P, P, I, I]
+        L.orc_int8_linear_dense.argtypes = [P, I64, I64, P, I64, P, I64, P, I, P]
         _lib = L
     return _lib
 
@@ -222,4 +225,33 @@ def attention_causal(q, k, v, dt: int, L: int, Hq: int, Hkv: int, D: int, qs: in
     rc = lib().orc_attention_causal(_p(q), _p(k), _p(v), dt, L, Hq, Hkv, D, qs, kvs, _p(out))
     if rc != 0:
         raise ValueError("attention_causal: D <= 256 and Hq a multiple of Hkv")
+    return out
+
+
+def rotq(x, dt: int, M: int, K: int, group: int):
+    """ConvRot rotation + per-row int8 quantisation (kernels/h3sycl.cpp:404-470 order): returns (xq [M, K] int8, rs [M])."""
+    xq = np.zeros((M, K), np.int8)
+    rs = np.zeros(M, np.float32)
+    lib().orc_rotq(_p(x), dt, M, K, group, _p(xq), _p(rs))
+    return xq, rs
+
+
+def int8_linear(x, dt: int, M: int, K: int, w: np.ndarray, N: int, wscale, bias, out_dt: int, group: int) -> np.ndarray:
+    """The int8 ConvRot linear (kernels/h3sycl.h:74-85, the fused kernel's rotation order): x [M, K] as element bits
+    of type dt; out [M, N] as bits (uint16) for F16/BF16, float32 for F32."""
+    out = np.zeros((M, N), np.float32 if out_dt == F32 else np.uint16)
+    ws = np.ascontiguousarray(wscale, np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    lib().orc_int8_linear(_p(np.ascontiguousarray(x)), dt, M, K, _p(np.ascontiguousarray(w, np.int8)), N, _p(ws), ws.size,
+                          _p(b), _p(out), out_dt, group)
+    return out
+
+
+def int8_linear_dense(x: np.ndarray, M: int, K: int, w: np.ndarray, N: int, wscale, bias, group: int) -> np.ndarray:
+    """engine/h3-core/src/reference.rs:37-82 as written (dense Hadamard product); x float32 [M, K]; out float32 [M, N]."""
+    out = np.zeros((M, N), np.float32)
+    ws = np.ascontiguousarray(wscale, np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    lib().orc_int8_linear_dense(_p(np.ascontiguousarray(x, np.float32)), M, K, _p(np.ascontiguousarray(w, np.int8)), N,
+                                _p(ws), ws.size, _p(b), group, _p(out))
     return out

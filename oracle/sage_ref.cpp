@@ -16,6 +16,11 @@
 //   fp16 fused SDPA    kernels/h3sycl.cpp:1464-1500 MatMul -> f32 scores, x f32 scale, SoftMax -> f16 P,
 //                                                   MatMul(P, v) -> f16   (oneDNN 3.12 graph, un-vendored)
 //   dispatcher         kernels/h3sycl.cpp:1779-1798 Sage when S >= sage_min_s (8192) and D in {64, 128}, else SDPA
+//   int8 ConvRot lin.  kernels/h3sycl.cpp:404-652   per row: Hadamard rotation per group, digit by digit in the order
+//                                                   of the fused kernel (:404-470), scale = max(max|x_rot|/127, 1e-30),
+//                                                   q = clamp(rint(x_rot/scale), -128, 127), int32 dots, then
+//                                                   acc * (scale*ws) [or (acc*scale)*ws[n]] + bias (:573-599);
+//                      engine/h3-core/src/reference.rs:37-82   the dense restatement as written (x_rot = x . H)
 //   causal GQA attn    kernels/h3sycl.cpp:870-898   per (head, query i): online softmax over keys j <= i in fp32,
 //                                                   s = (q.k) * 1/sqrt(D), exp, acc = acc*a + e*v, out = acc / l
 //   RMS norm + RoPE    kernels/h3sycl.cpp:1276-1376 per (token, head): s = sum of v*v in feature order,
@@ -27,6 +32,10 @@
 // :137-155). The quantiser and the attention arithmetic are UNPINNED: the reference has no test or fixture for them
 // and cannot be built here (SYCL + oneDNN + un-vendored ARK/sycl-tla). "Bit-exact" for the quantiser therefore means
 // bit-exact with this strict-IEEE restatement of the source order (build with -ffp-contract=off, no -ffast-math).
+// The int8 linear is checked against the reference's own tests of it (engine/h3-core/src/reference.rs:101-127: the
+// Hadamard matrix is orthonormal; the layer is within quantisation of a plain linear) and against the dense
+// restatement of reference.rs below; the butterfly's rounding order is the reference's fused kernel's, read from the
+// source (that kernel cannot run here).
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
@@ -444,6 +453,130 @@ int orc_attention_causal(const void* q, const void* k, const void* v, int dt, in
         for (int64_t d = 0; d < D; ++d) store(out, dt, (size_t) (i * Hq * D + h * D + d), acc[(size_t) d] / l);
     });
     return 0;
+}
+
+// ---- int8 ConvRot linear (kernels/h3sycl.cpp:404-652; engine/h3-core/src/reference.rs:37-82) ----------------------
+// The rotation of one group of g features in place, digit by digit (base 4) of the feature index, low digit first, as
+// the reference's fused kernel applies h4 for g = 256 (kernels/h3sycl.cpp:404-470): for the four values x_0..x_3 that
+// differ only in one digit, y_c = t - 2*x_(3-c). The sum t is ((x_0 + x_1) + x_2) + x_3 for the two low digits (inside
+// a lane that holds 16 consecutive features) and (x_0 + x_1) + (x_2 + x_3) for the higher ones (across lanes: lane c
+// forms (x_c + x_(c^1)) + (x_(c^2) + x_(c^3)), the same sum for every c); then the normalisation, 1/2 per digit.
+// g = 2 * 4^n (accepted by the reference, whose matrix builder, kernels/h3sycl.cpp:185-200, then gives the top digit
+// only the values 0 and 1, where h4's corner [[1, 1], [1, 1]] applies): y_0 = y_1 = x_0 + x_1 for that digit.
+static void rot_group(float* v, int g) {
+    int digit = 0;
+    for (int d = 1; d < g; d *= 4, ++digit) {
+        const bool in_thread = digit < 2;
+        if (4 * d > g) {
+            for (int e0 = 0; e0 < g; ++e0) {
+                if ((e0 / d) % 2 != 0) continue;
+                const float s = v[e0] + v[e0 + d];
+                v[e0] = s;
+                v[e0 + d] = s;
+            }
+            continue;
+        }
+        for (int e0 = 0; e0 < g; ++e0) {
+            if ((e0 / d) % 4 != 0) continue;
+            const float x[4] = {v[e0], v[e0 + d], v[e0 + 2 * d], v[e0 + 3 * d]};
+            float y[4];
+            if (in_thread) {
+                const float t = ((x[0] + x[1]) + x[2]) + x[3];
+                for (int c = 0; c < 4; ++c) y[c] = t - 2.0f * x[3 - c];
+            } else {
+                for (int c = 0; c < 4; ++c) {
+                    const float t = (x[c] + x[c ^ 1]) + (x[c ^ 2] + x[c ^ 3]);
+                    y[c] = t - 2.0f * x[c ^ 3];
+                }
+            }
+            for (int c = 0; c < 4; ++c) v[e0 + c * d] = y[c];
+        }
+    }
+    float norm = 1.0f;
+    for (int d = 1; d < g; d *= 4) norm *= 0.5f;
+    for (int e = 0; e < g; ++e) v[e] = v[e] * norm;
+}
+
+// Rotation (group 0: none) and per-row quantisation of x [M, K] (row stride K): xq int8 [M, K], rs [M] row scales.
+void orc_rotq(const void* x, int dt, int64_t M, int64_t K, int group, int8_t* xq, float* rs) {
+    par_for(M, 16, [&](int64_t r, int) {
+        std::vector<float> v((size_t) K);
+        for (int64_t i = 0; i < K; ++i) v[(size_t) i] = load(x, dt, (size_t) (r * K + i));
+        if (group > 0)
+            for (int64_t g0 = 0; g0 < K; g0 += group) rot_group(v.data() + g0, group);
+        float m = 0.0f;
+        for (int64_t i = 0; i < K; ++i) m = std::fmax(m, std::fabs(v[(size_t) i]));
+        const float scale = std::fmax(m / 127.0f, 1e-30f);
+        rs[r] = scale;
+        for (int64_t i = 0; i < K; ++i) {
+            const float q = std::nearbyint(v[(size_t) i] / scale);     // round half to even (the default mode)
+            xq[(size_t) (r * K + i)] = (int8_t) std::fmin(127.0f, std::fmax(-128.0f, q));
+        }
+    });
+}
+
+// The whole layer: rotation + quantisation as above, int32 products, then the reference's rescale (kernels/h3sycl.cpp
+// :573-599): one weight scale is folded into the row scale first (rs * ws, :573), so out = (float) acc * (rs * ws);
+// per-output scales multiply after the row scale, out = ((float) acc * rs) * ws[n]; the bias is added last; each step
+// rounded to float32, the result rounded to out_dt.
+void orc_int8_linear(const void* x, int dt, int64_t M, int64_t K, const int8_t* w, int64_t N, const float* wscale,
+                     int64_t n_wscale, const float* bias, void* out, int out_dt, int group) {
+    std::vector<int8_t> xq((size_t) (M * K));
+    std::vector<float> rs((size_t) M);
+    orc_rotq(x, dt, M, K, group, xq.data(), rs.data());
+    par_for(M, 4, [&](int64_t r, int) {
+        for (int64_t n = 0; n < N; ++n) {
+            int32_t acc = 0;
+            for (int64_t i = 0; i < K; ++i) acc += (int32_t) xq[(size_t) (r * K + i)] * (int32_t) w[(size_t) (n * K + i)];
+            float y = n_wscale > 1 ? ((float) acc * rs[(size_t) r]) * wscale[n] : (float) acc * (rs[(size_t) r] * wscale[0]);
+            if (bias) y = y + bias[n];
+            store(out, out_dt, (size_t) (r * N + n), y);
+        }
+    });
+}
+
+// engine/h3-core/src/reference.rs:37-82 as written there: x float32, the rotation a dense product with the normalised
+// regular Hadamard matrix (acc += x_i * H[i][j] in feature order), round half to even; out float32 [M, N]. Defined for
+// groups that are powers of 4 (reference.rs:4-5): its norm 1/sqrt(g) is the library's 2^-digits only there.
+void orc_int8_linear_dense(const float* x, int64_t M, int64_t K, const int8_t* w, int64_t N, const float* wscale,
+                           int64_t n_wscale, const float* bias, int group, float* out) {
+    std::vector<float> h;
+    if (group > 0) {
+        static const int h4[4][4] = {{1, 1, 1, -1}, {1, 1, -1, 1}, {1, -1, 1, 1}, {-1, 1, 1, 1}};
+        const float norm = 1.0f / std::sqrt((float) group);
+        h.resize((size_t) group * group);
+        for (int i = 0; i < group; ++i)
+            for (int j = 0; j < group; ++j) {
+                int sign = 1;
+                for (int a = i, b = j, st = 1; st < group; st *= 4, a /= 4, b /= 4) sign *= h4[a % 4][b % 4];
+                h[(size_t) i * group + j] = (float) sign * norm;
+            }
+    }
+    par_for(M, 4, [&](int64_t r, int) {
+        std::vector<float> xr((size_t) K);
+        const float* row = x + r * K;
+        if (group > 0) {
+            for (int64_t g0 = 0; g0 < K; g0 += group)
+                for (int j = 0; j < group; ++j) {
+                    float acc = 0.0f;
+                    for (int i = 0; i < group; ++i) acc += row[g0 + i] * h[(size_t) i * group + j];
+                    xr[(size_t) (g0 + j)] = acc;
+                }
+        } else {
+            for (int64_t i = 0; i < K; ++i) xr[(size_t) i] = row[i];
+        }
+        float m = 0.0f;
+        for (float v : xr) m = std::fmax(m, std::fabs(v));
+        const float scale = std::fmax(m / 127.0f, 1e-30f);
+        std::vector<int32_t> q((size_t) K);
+        for (int64_t i = 0; i < K; ++i) q[(size_t) i] = (int32_t) std::fmin(127.0f, std::fmax(-128.0f, std::nearbyint(xr[(size_t) i] / scale)));
+        for (int64_t n = 0; n < N; ++n) {
+            int32_t acc = 0;
+            for (int64_t i = 0; i < K; ++i) acc += (int32_t) w[(size_t) (n * K + i)] * q[(size_t) i];
+            const float ws = n_wscale == 1 ? wscale[0] : wscale[n];
+            out[(size_t) (r * N + n)] = (float) acc * scale * ws + (bias ? bias[n] : 0.0f);
+        }
+    });
 }
 
 }  // extern "C"

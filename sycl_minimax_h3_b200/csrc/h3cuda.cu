@@ -30,6 +30,7 @@
 #include "attn3.cuh"
 #include "rmsrope.cuh"
 #include "causal.cuh"
+#include "int8lin.cuh"
 
 namespace {
 
@@ -76,6 +77,10 @@ struct Ctx {
     __half* hk = nullptr; size_t hk_cap = 0;
     __half* hv = nullptr; size_t hv_cap = 0;
     __half* ao = nullptr; size_t ao_cap = 0;     // [H, S, D] output of a plugin without the strided entry
+    int8_t* lq = nullptr; size_t lq_cap = 0;     // int8 linear: quantised activations [rows, Kp]
+    float* lrs = nullptr; size_t lrs_cap = 0;    //   their row scales
+    int8_t* lw = nullptr; size_t lw_cap = 0;     //   the weight with rows padded to 16 bytes (K % 16 != 0 only)
+    int n_sm = 148;
     std::mutex mem_mu;
     std::unordered_map<void*, size_t> mem;
     size_t mem_used = 0, mem_cap = 0;
@@ -112,6 +117,7 @@ bool init(Ctx& c) {
     cudaDeviceProp p{};
     if (cudaGetDeviceProperties(&p, c.device) != cudaSuccess) { g_err = "cudaGetDeviceProperties failed"; return false; }
     c.name = p.name;
+    c.n_sm = p.multiProcessorCount;
     double frac = 0.94;
     if (const char* e = std::getenv("H3S_MEM_FRACTION")) frac = std::min(0.97, std::max(0.05, std::atof(e)));
     c.mem_cap = (size_t) ((double) p.totalGlobalMem * frac);
@@ -503,7 +509,7 @@ void h3s_destroy(void* ctx) {
     cudaStreamSynchronize(c->aux);
     if (c->cs) { cudaStreamSynchronize(c->cs); cudaStreamDestroy(c->cs); }
     for (void* p : {(void*) c->sq, (void*) c->sk, (void*) c->ss, (void*) c->hq, (void*) c->hk, (void*) c->hv, (void*) c->ao,
-                    (void*) c->err})
+                    (void*) c->lq, (void*) c->lrs, (void*) c->lw, (void*) c->err})
         if (p) cudaFree(p);
     for (auto& kv : c->mem) cudaFree(kv.first);
     cudaEventDestroy(c->ev_fork);
@@ -737,6 +743,79 @@ int h3s_rms_rope(void* ctx, void* x, int x_dt, int64_t M, int64_t H, int64_t D, 
         default: e = launch_rms_rope<F32>(x, M, (int) H, (int) D, stride, weight, eps, cs, rot_dim, c.st); break;
     }
     return e == cudaSuccess ? 0 : cuda_fail("h3s_rms_rope", e);
+}
+
+// kernels/h3sycl.cpp:632-652 (the entry point, its refusals and row chunks) and :404-630 (the layer), the arithmetic in
+// int8lin.cuh. Row chunks bound the int8 copy of the activations at 1 GiB.
+int h3s_int8_linear(void* ctx, const void* x, int x_dt, int64_t M, int64_t K, const int8_t* w, int64_t N,
+                    const float* wscale, int64_t n_wscale, const float* bias, void* out, int out_dt, int group) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    if (M <= 0 || K <= 0 || N <= 0) return 0;
+    if (group > 0 && (group > 256 || K % group != 0 || (group & (group - 1)) != 0)) {
+        g_err = "h3s_int8_linear: unsupported ConvRot group size";
+        return -1;
+    }
+    if (!check_dt(x_dt) || !check_dt(out_dt)) { g_err = "h3s_int8_linear: unknown element type"; return -1; }
+    if (n_wscale < 1 || (n_wscale > 1 && n_wscale < N)) {
+        g_err = "h3s_int8_linear: n_wscale must be 1 or N";
+        return -1;
+    }
+    if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX - 16) { g_err = "h3s_int8_linear: too large"; return -1; }
+    DeviceGuard g(c.device);
+    const int64_t Kp = (K + 15) / 16 * 16;
+    const int64_t rows_max = std::max<int64_t>(kLinBM, ((int64_t) 1 << 30) / Kp / kLinBM * kLinBM);
+    const int64_t n_nb = (N + kLinBN - 1) / kLinBN;
+    // the tile count of a chunk stays an int: rows x column blocks <= 2^30 tiles
+    const int64_t rows_tiles = std::max<int64_t>(kLinBM, ((int64_t) 1 << 30) / n_nb * kLinBM);
+    const int64_t R = std::min({M, rows_max, rows_tiles});
+    int8_t* xq = c.grow(c.lq, c.lq_cap, (size_t) (R * Kp));
+    float* rs = c.grow(c.lrs, c.lrs_cap, (size_t) R);
+    if (!xq || !rs) return -1;
+    cudaError_t e;
+    const int8_t* wk = w;
+    if (K != Kp || (reinterpret_cast<uintptr_t>(w) & 15)) {
+        int8_t* wp = c.grow(c.lw, c.lw_cap, (size_t) (N * Kp));
+        if (!wp) return -1;
+        pad_rows_i8<<<c.n_sm * 4, 256, 0, c.st>>>(w, (int) N, (int) K, (int) Kp, wp);
+        if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("h3s_int8_linear", e);
+        wk = wp;
+    }
+    CUtensorMap tb;
+    std::string why = make_i8_map(&tb, wk, Kp, N, Kp, kLinBN);
+    if (!why.empty()) { g_err = "h3s_int8_linear: weight map: " + why; return -1; }
+    LinArgs a{};
+    a.N = (int) N;
+    a.nkb = (int) ((Kp + kLinBK - 1) / kLinBK);
+    a.n_nb = (int) n_nb;
+    // a band of column blocks whose slice of W (256 rows x Kp bytes each) takes at most 64 MiB of L2
+    a.band = (int) std::max<int64_t>(1, std::min<int64_t>(a.n_nb, ((int64_t) 64 << 20) / (kLinBN * Kp)));
+    a.rs = rs;
+    a.ws = wscale;
+    a.per_n = n_wscale > 1;
+    a.bias = bias;
+    a.out_dt = out_dt;
+    a.err = c.err;
+    a.wait_ns = c.wait_ns;
+    const size_t xe = x_dt == F32 ? 4 : 2, oe = out_dt == F32 ? 4 : 2;
+    for (int64_t r0 = 0; r0 < M; r0 += R) {
+        const int rows = (int) std::min(R, M - r0);
+        const void* xr = static_cast<const char*>(x) + (size_t) r0 * K * xe;
+        switch (x_dt) {
+            case F16: e = launch_rotq<F16>(xr, rows, (int) K, (int) Kp, group, xq, rs, c.n_sm, c.st); break;
+            case BF16: e = launch_rotq<BF16>(xr, rows, (int) K, (int) Kp, group, xq, rs, c.n_sm, c.st); break;
+            default: e = launch_rotq<F32>(xr, rows, (int) K, (int) Kp, group, xq, rs, c.n_sm, c.st); break;
+        }
+        if (e != cudaSuccess) return cuda_fail("h3s_int8_linear", e);
+        CUtensorMap ta;
+        why = make_i8_map(&ta, xq, Kp, rows, Kp, kLinBM);
+        if (!why.empty()) { g_err = "h3s_int8_linear: activation map: " + why; return -1; }
+        a.M = rows;
+        a.n_mb = (rows + kLinBM - 1) / kLinBM;
+        a.out = static_cast<char*>(out) + (size_t) r0 * N * oe;
+        a.out_vec = (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && ((size_t) N * oe) % 16 == 0;
+        if ((e = launch_i8gemm(ta, tb, a, c.n_sm, c.st)) != cudaSuccess) return cuda_fail("h3s_int8_linear", e);
+    }
+    return 0;
 }
 
 int h3s_sage_prepass(void* ctx, const void* q, const void* k, int dt, int64_t S, int64_t H, int64_t D, int64_t stride,

@@ -44,6 +44,7 @@ CUDA_SYMBOLS = [
     ("h3s_attention_batch", I, [P, P, P, P, I, I64, I64, I64, I64, I64, P, I]),
     ("h3s_rms_rope", I, [P, P, I, I64, I64, I64, I64, P, ctypes.c_float, P, I]),
     ("h3s_attention_causal", I, [P, P, P, P, I, I64, I64, I64, I64, I64, I64, P]),
+    ("h3s_int8_linear", I, [P, P, I, I64, I64, P, I64, P, I64, P, P, I, I]),
     ("h3s_sage_prepass", I, [P, P, P, I, I64, I64, I64, I64, P, P, P]),
     ("h3s_stream", P, [P]),
     ("h3s_selftest_wait_timeout", I, [P, U64]),
@@ -198,6 +199,11 @@ class Context:
     def rms_rope(self, x: int, dt: int, M: int, H: int, D: int, stride: int, weight: int, eps: float, cs: int,
                  rot_dim: int) -> None:
         check(self._lib.h3s_rms_rope(self.handle, x, dt, M, H, D, stride, weight, eps, cs, rot_dim), "h3s_rms_rope")
+
+    def int8_linear(self, x: int, x_dt: int, M: int, K: int, w: int, N: int, wscale: int, n_wscale: int, bias: int,
+                    out: int, out_dt: int, group: int) -> None:
+        check(self._lib.h3s_int8_linear(self.handle, x, x_dt, M, K, w, N, wscale, n_wscale, bias, out, out_dt, group),
+              "h3s_int8_linear")
 
     def attention_causal(self, q: int, k: int, v: int, dt: int, L: int, Hq: int, Hkv: int, D: int, qs: int, kvs: int,
                          out: int) -> None:

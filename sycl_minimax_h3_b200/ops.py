@@ -81,6 +81,43 @@ def rms_rope(x: Rows, weight: torch.Tensor, eps: float, cs: torch.Tensor, rot_di
                  rot_dim)
 
 
+@dataclass(frozen=True)
+class Int8Linear:
+    """A linear layer with int8 weights (one layer of an ``int8_convrot`` checkpoint), on the device (ops.rs:25-80):
+    ``weight`` int8 [N, K], ``scale`` float32 with 1 or N values, ``bias`` float32 [N] or None, ``group`` the rotation
+    group size when the weights were stored rotated."""
+
+    weight: torch.Tensor
+    scale: torch.Tensor
+    bias: torch.Tensor | None = None
+    group: int | None = None
+
+    def inputs(self) -> int:
+        return self.weight.shape[1]
+
+    def outputs(self) -> int:
+        return self.weight.shape[0]
+
+    def forward(self, x: torch.Tensor, out: torch.Tensor) -> None:
+        """``out = linear(x)``: x [M, K] in a float type, out [M, N] in out's type (ops.rs:45-79)."""
+        n, k = self.outputs(), self.inputs()
+        m = x.numel() // k
+        if self.weight.dtype != torch.int8 or self.scale.dtype != torch.float32:
+            raise H3Error("int8_linear: the weight must be int8 and its scale float32")
+        if x.numel() != m * k or out.numel() != m * n:
+            raise H3Error(f"int8_linear: x {list(x.shape)} and out {list(out.shape)} do not fit a [{n}, {k}] weight")
+        ns = self.scale.numel()
+        if ns != 1 and ns != n:
+            raise H3Error(f"int8_linear: {ns} weight scales for {n} outputs")
+        for t, what in ((x, "x"), (out, "out"), (self.weight, "the weight"), (self.scale, "the scale")):
+            if not t.is_contiguous():
+                raise H3Error(f"int8_linear: {what} must be contiguous")
+        bias = _floats(self.bias, "the bias", n) if self.bias is not None else 0
+        ctx = context(out.device)
+        ctx.int8_linear(x.data_ptr(), dt_code(x.dtype), m, k, self.weight.data_ptr(), n, self.scale.data_ptr(), ns,
+                        bias, out.data_ptr(), dt_code(out.dtype), self.group or 0)
+
+
 def attention_causal(q: Rows, k: Rows, v: Rows, out: torch.Tensor) -> None:
     """Causal attention with grouped heads (the text encoder's call, te.rs:340-346): q has the query heads, k and v the
     key/value heads (a divisor of them), all with the same tokens and head size; out [tokens, q.heads * dim] in q's

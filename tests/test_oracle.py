@@ -288,3 +288,104 @@ def test_causal_refusals(orc):
         orc.attention_causal(x, x, x, orc.F32, 2, 1, 1, 512, 512, 512)      # D > 256
     with pytest.raises(ValueError):
         orc.attention_causal(x, x, x, orc.F32, 2, 3, 2, 128, 512, 512)      # Hq not a multiple of Hkv
+
+
+# ---- int8 ConvRot linear (kernels/h3sycl.cpp:404-652; engine/h3-core/src/reference.rs:37-132) ----------------------
+def _hadamard(g):
+    """The reference's normalised Hadamard matrix builder (kernels/h3sycl.cpp:185-200), in float64."""
+    h4 = np.array([[1, 1, 1, -1], [1, 1, -1, 1], [1, -1, 1, 1], [-1, 1, 1, 1]])
+    h = np.zeros((g, g))
+    norm = 1.0
+    s = 1
+    while s < g:
+        norm *= 0.5
+        s *= 4
+    for i in range(g):
+        for j in range(g):
+            sign, a, b, s = 1, i, j, 1
+            while s < g:
+                sign *= h4[a % 4][b % 4]
+                a, b, s = a // 4, b // 4, s * 4
+            h[i, j] = sign * norm
+    return h
+
+
+def _compare(a, b):
+    """reference.rs:85-95: relative error and cosine."""
+    a, b = a.astype(np.float64).ravel(), b.astype(np.float64).ravel()
+    return np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-300), a @ b / max(np.linalg.norm(a) * np.linalg.norm(b), 1e-300)
+
+
+@pytest.mark.parametrize("g", [4, 16, 64])
+def test_hadamard_is_orthonormal(g):
+    """reference.rs:105-113."""
+    h = _hadamard(g)
+    assert np.allclose(h @ h.T, np.eye(g), atol=1e-12)
+
+
+def test_int8_linear_matches_a_plain_linear_within_quantization(orc):
+    """reference.rs:115-127 on both restatements: weights exactly int8 * scale, no rotation."""
+    m, k, n = 3, 64, 5
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    w = rng.integers(-127, 128, (n, k)).astype(np.int8)
+    ws = np.array([0.01], np.float32)
+    want = (x.astype(np.float64) @ w.astype(np.float64).T) * 0.01
+    for got in (orc.int8_linear_dense(x, m, k, w, n, ws, None, 0),
+                orc.int8_linear(x, orc.F32, m, k, w, n, ws, None, orc.F32, 0)):
+        rel, cos = _compare(got, want)
+        assert rel < 0.02 and cos > 0.999, (rel, cos)
+
+
+@pytest.mark.parametrize("g", [2, 4, 8, 16, 32, 64, 128, 256])
+def test_butterfly_matches_the_dense_rotation(orc, g):
+    """The butterfly (the fused kernel's order) against the dense rotation with the matrix the library builds
+    (kernels/h3sycl.cpp:185-200), for every group the entry point accepts (2 * 4^n included, where that matrix is
+    singular in its top digit and its norm is 1/2 per base-4 digit), and against reference.rs's dense product for the
+    powers of 4 it is defined on (reference.rs:4-5; its norm 1/sqrt(g) is the library's there): the rotated values
+    differ by float rounding only, so at most a few quantisation levels move, by one."""
+    M, K, N = 16, 1024, 24
+    rng = np.random.default_rng(g)
+    x = (rng.standard_normal((M, K)) * 3).astype(np.float32)
+    w = rng.integers(-127, 128, (N, K)).astype(np.int8)
+    ws = (rng.random(N) * 0.01 + 1e-3).astype(np.float32)
+    b = rng.standard_normal(N).astype(np.float32)
+    a = orc.int8_linear(x, orc.F32, M, K, w, N, ws, b, orc.F32, g)
+    if g in (4, 16, 64, 256):
+        d = orc.int8_linear_dense(x, M, K, w, N, ws, b, g)
+        rel, cos = _compare(a, d)
+        assert rel < 2e-3 and cos > 0.99999, (rel, cos)
+    # and the float64 rotation with the reference's matrix, quantised the same way, agrees as closely
+    xr = (x.astype(np.float64).reshape(M, K // g, g) @ _hadamard(g)).reshape(M, K)
+    s = np.maximum(np.abs(xr).max(1) / 127, 1e-30)
+    q = np.clip(np.rint(xr / s[:, None]), -128, 127)
+    exact = (q @ w.astype(np.float64).T) * s[:, None] * ws[None, :] + b[None, :]
+    rel, _ = _compare(a, exact)
+    assert rel < 2e-3, rel
+
+
+def test_rotated_weights_recover_the_plain_linear(orc):
+    """With W stored rotated (W . H per group, quantised per output row) the rotation cancels: the layer is within
+    quantisation of x . W^T (what int8_convrot checkpoints rely on)."""
+    M, K, N, g = 8, 512, 32, 256
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    wf = rng.standard_normal((N, K)) / 16
+    wr = (wf.reshape(N, K // g, g) @ _hadamard(g)).reshape(N, K)
+    sc = np.abs(wr).max(1) / 127
+    wq = np.clip(np.rint(wr / sc[:, None]), -127, 127).astype(np.int8)
+    got = orc.int8_linear(x, orc.F32, M, K, wq, N, sc.astype(np.float32), None, orc.F32, g)
+    rel, cos = _compare(got, x.astype(np.float64) @ wf.T)
+    assert rel < 0.02 and cos > 0.999, (rel, cos)
+
+
+def test_rotq_scale_and_clamp(orc):
+    """Row scale = max(absmax / 127, 1e-30); the largest value of a row quantises to +-127; a zero row keeps the floor
+    scale and all-zero codes."""
+    x = np.zeros((3, 64), np.float32)
+    x[1] = np.linspace(-5, 3, 64)
+    x[2, 5] = 1e-20
+    q, s = orc.rotq(x, orc.F32, 3, 64, 0)
+    assert s[0] == np.float32(1e-30) and not q[0].any()
+    assert s[1] == np.float32(np.float32(5) / np.float32(127)) and q[1, 0] == -127 and q[1].max() <= 127
+    assert q[2, 5] == 127
