@@ -597,7 +597,8 @@ def int8_linear_leg(dev, M, peaks, max_over_ranks, barrier, K=4096, N=12288, gro
     ms = max_over_ranks(e0.elapsed_time(e1)) / n
     tops = 2.0 * M * N * K / (ms / 1e3) / 1e12
     peak = 2 * peaks["bf16_tflops"]
-    return {"kernels": "rotq_rows<bf16,256> + i8gemm (tcgen05 kind::i8, 128x256 tiles)", "M": M, "K": K, "N": N,
+    return {"kernels": "rotq_rows<bf16,256> + i8gemm2 (tcgen05.mma cta_group::2 kind::i8, 256x256 tiles per SM pair)",
+            "M": M, "K": K, "N": N,
             "group": group, "ms": ms, "tops": tops, "peak_int8_tops": peak, "peak_source": peaks["source"],
             "frac": tops / peak}
 

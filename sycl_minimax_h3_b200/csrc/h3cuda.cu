@@ -781,7 +781,7 @@ int h3s_int8_linear(void* ctx, const void* x, int x_dt, int64_t M, int64_t K, co
         wk = wp;
     }
     CUtensorMap tb;
-    std::string why = make_i8_map(&tb, wk, Kp, N, Kp, kLinBN);
+    std::string why = make_i8_map(&tb, wk, Kp, N, Kp, lin_weight_rows());
     if (!why.empty()) { g_err = "h3s_int8_linear: weight map: " + why; return -1; }
     LinArgs a{};
     a.N = (int) N;
@@ -810,7 +810,7 @@ int h3s_int8_linear(void* ctx, const void* x, int x_dt, int64_t M, int64_t K, co
         why = make_i8_map(&ta, xq, Kp, rows, Kp, kLinBM);
         if (!why.empty()) { g_err = "h3s_int8_linear: activation map: " + why; return -1; }
         a.M = rows;
-        a.n_mb = (rows + kLinBM - 1) / kLinBM;
+        a.n_mb = (rows + lin_rows_per_tile() - 1) / lin_rows_per_tile();
         a.out = static_cast<char*>(out) + (size_t) r0 * N * oe;
         a.out_vec = (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && ((size_t) N * oe) % 16 == 0;
         if ((e = launch_i8gemm(ta, tb, a, c.n_sm, c.st)) != cudaSuccess) return cuda_fail("h3s_int8_linear", e);

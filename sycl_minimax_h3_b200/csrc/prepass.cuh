@@ -32,10 +32,9 @@ __device__ __forceinline__ float ld1(const void* p, size_t i) {
     else if constexpr (DT == BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
     else return reinterpret_cast<const float*>(p)[i];
 }
-// 16 bytes -> 16/ES floats
+// 16 bytes (as loaded) -> 16/ES floats
 template <int DT>
-__device__ __forceinline__ void ld16(const void* p, float* out) {
-    const uint4 u = *reinterpret_cast<const uint4*>(p);
+__device__ __forceinline__ void cvt16(const uint4 u, float* out) {
     if constexpr (DT == F32) {
         out[0] = __uint_as_float(u.x); out[1] = __uint_as_float(u.y); out[2] = __uint_as_float(u.z); out[3] = __uint_as_float(u.w);
     } else {
@@ -52,6 +51,11 @@ __device__ __forceinline__ void ld16(const void* p, float* out) {
             }
         }
     }
+}
+// 16 bytes at p -> 16/ES floats
+template <int DT>
+__device__ __forceinline__ void ld16(const void* p, float* out) {
+    cvt16<DT>(*reinterpret_cast<const uint4*>(p), out);
 }
 
 // ---- K mean, TMA ring ----------------------------------------------------------------------------------------------

@@ -245,6 +245,72 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
     return d;
 }
 
+// ---- CTA pairs (clusters of 2) and tcgen05 with cta_group::2 -------------------------------------------------------
+// In a cluster of two CTAs, one tcgen05.mma.cta_group::2 issued by rank 0 computes a 256-row tile: A's rows 0-127 and
+// the first half of B's rows come from rank 0's shared memory, the rest from rank 1's at the same offsets, and each
+// CTA's tensor memory receives its own 128 rows of D. Barriers of the other CTA are reached through mapa addresses.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// the shared::cluster address of the object at `saddr` (a shared::cta address of this CTA) in CTA `rank`'s memory
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+    uint32_t d;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
+    return d;
+}
+// every thread of both CTAs; orders the barrier initialisation (and everything else before it) for the other CTA
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t ld_shared_cluster(uint32_t caddr) {
+    uint32_t v;
+    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(caddr) : "memory");
+    return v;
+}
+// one arrival on an mbarrier given by its shared::cluster address (this CTA's or the other's)
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t caddr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+// A TMA load into this CTA's shared memory whose completion is counted on the mbarrier at `bar_caddr`, which may be
+// the other CTA's (cta_group::2). Never with multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar_caddr, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_caddr), "r"(c0), "r"(c1)
+        : "memory");
+}
+// allocation by one warp of each CTA of the pair (the same warp index, the same destination offset)
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// warp-wide, one elected lane issues: D (256 rows over the pair) (+)= A . B^T, kind::i8
+__device__ __forceinline__ void mma_pair_i8_w(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t.reg .b32 r;\n\telect.sync r|e, 0xffffffff;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// warp-wide, the same elected lane as the MMAs: one arrival on the mbarrier at `bar_caddr` (either CTA's) once every
+// tcgen05 operation the lane issued before has completed
+__device__ __forceinline__ void mma_commit_pair_w(uint32_t bar_caddr) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\telect.sync r|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(bar_caddr)
+        : "memory");
+}
+
 // ---- UMMA descriptors ----------------------------------------------------------------------------------------------
 // Shared-memory matrix descriptor: start address, leading / stride byte offsets (all >> 4), version 1 (sm_100),
 // base offset 0 (atoms 1024-byte aligned), layout type in bits 61-63 (2 = 128-byte swizzle).

@@ -155,6 +155,29 @@ def test_rotated_weights_match_a_plain_linear(cuda):
     assert rel < 0.02 and cos > 0.999, (rel, cos)
 
 
+def test_quantiser_ties(cuda):
+    """Quotients exactly on a half (round half to even: 0.5 -> 0, 1.5 -> 2, -2.5 -> -2) and one float step either side
+    of it, read through an identity weight (out = the int8 codes times the row scale). Rows 0-1 have scales 1 and 2
+    (max 127 and 254), so the quotients are exact; rows 2-3 sit one step off the halves; the rest are random."""
+    K = 256
+    x = np.random.default_rng(2).standard_normal((6, K)).astype(np.float32) * 3
+    halves = np.arange(-127, 127, dtype=np.float32) + np.float32(0.5)      # -126.5 .. 126.5: columns 1-254
+    x[:4, 255] = 0
+    x[0, 0], x[0, 1:255] = 127, halves
+    x[1, 0], x[1, 1:255] = 254, 2 * halves
+    x[2, 0], x[2, 1:255] = 127, np.nextafter(halves, np.float32(np.inf))
+    x[3, 0], x[3, 1:255] = 127, np.nextafter(halves, np.float32(-np.inf))
+    xt = torch.from_numpy(x)
+    w = torch.eye(K, dtype=torch.int8)
+    ws = torch.ones(1)
+    got = run(xt, w, ws, None, torch.float32, 0, cuda).cpu().numpy()
+    want = expect(xt, w, ws, None, torch.float32, 0)
+    assert np.array_equal(got, want)
+    codes = np.rint(halves.astype(np.float64))
+    assert np.array_equal(got[0, 1:255], codes) and np.array_equal(got[1, 1:255], 2 * codes)
+    assert np.array_equal(got[2, 1:255], np.ceil(halves)) and np.array_equal(got[3, 1:255], np.floor(halves))
+
+
 def test_refusals_and_degenerate_sizes(cuda):
     ctx = ops.context(cuda)
     x = torch.randn(4, 64, device=cuda).half()
