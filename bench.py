@@ -177,7 +177,7 @@ def main() -> None:
     ap.add_argument("--quick", action="store_true", help="main workload only (no c1/c2/c4 side numbers)")
     ap.add_argument("--S", type=int, default=47232, help="tokens of the main workload (profiling runs use a smaller case)")
     ap.add_argument("--H", type=int, default=32, help="heads of the main workload")
-    ap.add_argument("--only", choices=["c1", "c2", "rms_rope", "causal", "int8_linear"],
+    ap.add_argument("--only", choices=["c1", "c2", "rms_rope", "causal", "int8_linear", "vae"],
                     help="run one side leg alone and print its numbers (for profiling that kernel); no bench line")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -222,6 +222,8 @@ def main() -> None:
             res = causal_leg(dev, max_over_ranks, barrier)
         elif args.only == "int8_linear":
             res = int8_linear_leg(dev, S, peaks, max_over_ranks, barrier)
+        elif args.only == "vae":
+            res = vae_leg(dev, max_over_ranks, barrier)
         elif args.only == "rms_rope":
             g = torch.Generator(device=dev)
             g.manual_seed(1000)
@@ -421,6 +423,7 @@ def main() -> None:
         extra["rms_rope"] = rms_rope_leg(dev, pool[0], S, h, D, peaks, max_over_ranks, barrier)
         extra["causal"] = causal_leg(dev, max_over_ranks, barrier)
         extra["int8_linear"] = int8_linear_leg(dev, S, peaks, max_over_ranks, barrier)
+        extra["vae"] = vae_leg(dev, max_over_ranks, barrier)
         if world > 1:
             extra["c4_ulysses"] = ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier)
 
@@ -601,6 +604,39 @@ def int8_linear_leg(dev, M, peaks, max_over_ranks, barrier, K=4096, N=12288, gro
             "M": M, "K": K, "N": N,
             "group": group, "ms": ms, "tops": tops, "peak_int8_tops": peak, "peak_source": peaks["source"],
             "frac": tops / peak}
+
+
+def vae_leg(dev, max_over_ranks, barrier, B=4, S=1797, H=32, D=64) -> dict:
+    """The VAE decoder's attention (h3s_attention_batch, vae.rs:309-311): a batch of B = 4 tiles (TILE_BATCH) of
+    S = 1,797 tokens (7 x 16 x 16 latent cells + 4 registers + 1), 32 heads of 64 (vae.rs:21-22), fp16 q/k/v read in
+    place from the qkv buffer (row stride 3 x 2048) and fp16 out; each tile attends to its own tokens (fp16 SDPA path).
+    Seeded normal values stand in for the decoder's activations. Work: 4*S^2*D*H*B flops."""
+    import torch
+
+    from sycl_minimax_h3_b200 import ops
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(64)
+    qkv = torch.randn(B * S, 3 * H * D, generator=g, device=dev, dtype=torch.float16)
+    out = torch.empty(B * S, H * D, device=dev, dtype=torch.float16)
+    q, k, v = ops.Rows.qkv(qkv, H, D)
+    for _ in range(3):
+        ops.attention_batch(q, k, v, B, out)
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 20
+    e0.record(torch.cuda.current_stream())
+    for _ in range(n):
+        ops.attention_batch(q, k, v, B, out)
+    e1.record(torch.cuda.current_stream())
+    torch.cuda.synchronize()
+    ops.context(dev).wait()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1)) / n
+    flops = 4.0 * S * S * D * H * B
+    return {"kernel": "attn_sage3<false> (fp16 SDPA, batch in the grid)", "B": B, "S": S, "H": H, "D": D, "ms": ms,
+            "tflops": flops / (ms / 1e3) / 1e12}
 
 
 def ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier) -> dict:
