@@ -640,7 +640,9 @@ def vae_leg(dev, max_over_ranks, barrier, B=4, S=1797, H=32, D=64) -> dict:
 
 
 def ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier) -> dict:
-    """c4: token-sharded qkv -> all-to-all -> attention of H/P heads over all S tokens -> inverse all-to-all."""
+    """c4: token-sharded qkv -> all-to-all -> attention of H/P heads over all S tokens -> inverse all-to-all. The
+    exchange is ulysses.PeerExchange (each rank stores its data straight into the other ranks' buffers over NVLink,
+    relayout included); NCCL's all_to_all_single with the relayout copies around it is timed beside it."""
     import torch
 
     from sycl_minimax_h3_b200 import ops, ulysses
@@ -651,37 +653,45 @@ def ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier) -> dict:
     shard = torch.randn(s, 3 * H * D, generator=g, device=dev, dtype=torch.float16)
     h = H // world
     out = torch.empty(S, h * D, dtype=torch.float16, device=dev)
+    ex = ulysses.PeerExchange(s, H, D, torch.float16)
 
-    def step(times=None):
+    def step(peer, times=None):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
         ev[0].record()
-        qkv_heads = ulysses.seq_to_heads(shard, H, D)
+        qkv_heads = ex.seq_to_heads(shard) if peer else ulysses.seq_to_heads(shard, H, D)
         ev[1].record()
         q, k, v = ops.Rows.qkv(qkv_heads, h, D)
         ops.attention(q, k, v, out)
         ev[2].record()
-        res = ulysses.heads_to_seq(out, H, D)
+        res = ex.heads_to_seq(out) if peer else ulysses.heads_to_seq(out, H, D)
         ev[3].record()
         if times is not None:
             times.append(ev)
         return res
 
-    for _ in range(3):
-        step()
-    torch.cuda.synchronize()
-    barrier()
-    times = []
-    n = 10
-    for _ in range(n):
-        step(times)
-    torch.cuda.synchronize()
-    ops.context(dev).wait()
-    a2a = sum(e[0].elapsed_time(e[1]) + e[2].elapsed_time(e[3]) for e in times) / n
-    att = sum(e[1].elapsed_time(e[2]) for e in times) / n
-    tot = sum(e[0].elapsed_time(e[3]) for e in times) / n
-    return {"tokens_per_gpu": s, "heads_per_gpu": h, "ms_per_call": max_over_ranks(tot),
-            "ms_all_to_all_exposed": max_over_ranks(a2a), "ms_attention": max_over_ranks(att),
-            "tops": ops_per_call(S, H, D) / (max_over_ranks(tot) / 1e3) / 1e12}
+    def measure(peer):
+        for _ in range(3):
+            step(peer)
+        torch.cuda.synchronize()
+        barrier()
+        times = []
+        n = 10
+        for _ in range(n):
+            step(peer, times)
+        torch.cuda.synchronize()
+        ops.context(dev).wait()
+        a2a = sum(e[0].elapsed_time(e[1]) + e[2].elapsed_time(e[3]) for e in times) / n
+        att = sum(e[1].elapsed_time(e[2]) for e in times) / n
+        tot = sum(e[0].elapsed_time(e[3]) for e in times) / n
+        return max_over_ranks(tot), max_over_ranks(a2a), max_over_ranks(att)
+
+    tot, a2a, att = measure(True)
+    tot_n, a2a_n, _ = measure(False)
+    ex.close()
+    return {"tokens_per_gpu": s, "heads_per_gpu": h, "exchange": "peer stores over NVLink (CUDA IPC)",
+            "ms_per_call": tot, "ms_all_to_all_exposed": a2a, "ms_attention": att,
+            "tops": ops_per_call(S, H, D) / (tot / 1e3) / 1e12,
+            "nccl_all_to_all": {"ms_per_call": tot_n, "ms_all_to_all_exposed": a2a_n}}
 
 
 if __name__ == "__main__":

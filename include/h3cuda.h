@@ -142,6 +142,25 @@ int h3s_attention_causal(void* ctx, const void* q, const void* k, const void* v,
 
 /* ---- additions without a counterpart in the reference ----------------------------------------------------------- */
 
+/* The Ulysses exchange over peer memory, for one process per GPU on one node (NVLink/NVSwitch): a sequence of S
+ * tokens sharded by tokens over P ranks (s = S/P rows each) is re-sharded by heads (h = H/P each) for the attention
+ * and back, each rank storing straight into the other ranks' buffers.
+ * h3s_ipc_handle: the 64-byte CUDA IPC handle of a buffer from h3s_alloc (its base pointer). h3s_ipc_open: another
+ * process's buffer from its handle (NULL on failure); h3s_ipc_close undoes it. */
+int h3s_ipc_handle(void* ctx, const void* ptr, void* handle);
+void* h3s_ipc_open(void* ctx, const void* handle);
+int h3s_ipc_close(void* ctx, void* ptr);
+/* Forward: this rank's token rows of a qkv buffer, shard [s, 3*H*D] (q | k | v, es-byte elements: 2 or 4), into every
+ * rank p's head-sharded buffer dst[p] = [P*s, 3*h*D]: heads p*h .. p*h+h-1 of each part, at rows rank*s .. rank*s+s-1.
+ * Inverse: this rank's output out_heads [P*s, h*D] into every rank p's token rows dst[p] = [s, H*D] at columns
+ * rank*h*D ... dst[rank] is this rank's own buffer, the others opened with h3s_ipc_open; P <= 8, H a multiple of P.
+ * Queued on the context's stream; the ranks must meet (a collective on the same streams) before they overwrite what
+ * another rank still reads and before they read what they received. */
+int h3s_ulysses_push_qkv(void* ctx, const void* shard, int64_t s, int64_t H, int64_t D, int es, int P, int rank,
+                         void* const* dst);
+int h3s_ulysses_push_out(void* ctx, const void* out_heads, int64_t s, int64_t H, int64_t D, int es, int P, int rank,
+                         void* const* dst);
+
 /* The Sage pre-pass alone (kernels/h3sycl.cpp:1733-1761 as a callable step, for parity checks and for callers that
  * keep int8 q/k): iq, ik int8 [H, S, D]; sc float [2*H*nb + H*D] = q scales [H, nb], k scales [H, nb], k's channel
  * mean [H*D], nb = ceil(S / 64). D = 64 or 128. Queued on the context's stream. */

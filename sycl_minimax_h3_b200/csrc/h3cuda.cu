@@ -31,6 +31,7 @@
 #include "rmsrope.cuh"
 #include "causal.cuh"
 #include "int8lin.cuh"
+#include "ulysses.cuh"
 
 namespace {
 
@@ -816,6 +817,77 @@ int h3s_int8_linear(void* ctx, const void* x, int x_dt, int64_t M, int64_t K, co
         if ((e = launch_i8gemm(ta, tb, a, c.n_sm, c.st)) != cudaSuccess) return cuda_fail("h3s_int8_linear", e);
     }
     return 0;
+}
+
+// ---- the Ulysses exchange over peer memory (ulysses.cuh) ------------------------------------------------------------
+int h3s_ipc_handle(void* ctx, const void* ptr, void* handle) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    if (!ptr || !handle) { g_err = "h3s_ipc_handle: null pointer"; return -1; }
+    DeviceGuard g(c.device);
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+    if (e != cudaSuccess) return cuda_fail("h3s_ipc_handle", e);
+    static_assert(sizeof(h) == 64, "a CUDA IPC handle is 64 bytes");
+    std::memcpy(handle, &h, sizeof(h));
+    return 0;
+}
+
+void* h3s_ipc_open(void* ctx, const void* handle) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    if (!handle) { g_err = "h3s_ipc_open: null handle"; return nullptr; }
+    DeviceGuard g(c.device);
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void* p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) { cuda_fail("h3s_ipc_open", e); return nullptr; }
+    return p;
+}
+
+int h3s_ipc_close(void* ctx, void* ptr) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    if (!ptr) return 0;
+    DeviceGuard g(c.device);
+    cudaStreamSynchronize(c.st);
+    const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+    return e == cudaSuccess ? 0 : cuda_fail("h3s_ipc_close", e);
+}
+
+// the checks both directions share; fills the peer table
+static int ulysses_args(const char* what, int64_t s, int64_t H, int64_t D, int es, int P, int rank, void* const* dst,
+                        PeerBases& pb) {
+    if (P < 1 || P > kMaxPeers || rank < 0 || rank >= P) { g_err = std::string(what) + ": 1 to 8 ranks"; return -1; }
+    if (s <= 0 || H <= 0 || D <= 0 || H % P != 0 || (es != 2 && es != 4)) {
+        g_err = std::string(what) + ": s, H, D > 0, H a multiple of the ranks, 2- or 4-byte elements";
+        return -1;
+    }
+    if (!dst) { g_err = std::string(what) + ": no destination table"; return -1; }
+    for (int p = 0; p < kMaxPeers; ++p) pb.p[p] = p < P ? static_cast<char*>(dst[p]) : nullptr;
+    for (int p = 0; p < P; ++p)
+        if (!pb.p[p]) { g_err = std::string(what) + ": destination " + std::to_string(p) + " is null"; return -1; }
+    return 0;
+}
+
+int h3s_ulysses_push_qkv(void* ctx, const void* shard, int64_t s, int64_t H, int64_t D, int es, int P, int rank,
+                         void* const* dst) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    PeerBases pb;
+    if (ulysses_args("h3s_ulysses_push_qkv", s, H, D, es, P, rank, dst, pb) != 0) return -1;
+    if (!shard) { g_err = "h3s_ulysses_push_qkv: null shard"; return -1; }
+    DeviceGuard g(c.device);
+    const cudaError_t e = launch_push_qkv(shard, s, (int) H, (int) D, es, P, rank, pb, c.n_sm, c.st);
+    return e == cudaSuccess ? 0 : cuda_fail("h3s_ulysses_push_qkv", e);
+}
+
+int h3s_ulysses_push_out(void* ctx, const void* out_heads, int64_t s, int64_t H, int64_t D, int es, int P, int rank,
+                         void* const* dst) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    PeerBases pb;
+    if (ulysses_args("h3s_ulysses_push_out", s, H, D, es, P, rank, dst, pb) != 0) return -1;
+    if (!out_heads) { g_err = "h3s_ulysses_push_out: null output"; return -1; }
+    DeviceGuard g(c.device);
+    const cudaError_t e = launch_push_out(out_heads, s, (int) H, (int) D, es, P, rank, pb, c.n_sm, c.st);
+    return e == cudaSuccess ? 0 : cuda_fail("h3s_ulysses_push_out", e);
 }
 
 int h3s_sage_prepass(void* ctx, const void* q, const void* k, int dt, int64_t S, int64_t H, int64_t D, int64_t stride,

@@ -45,6 +45,11 @@ CUDA_SYMBOLS = [
     ("h3s_rms_rope", I, [P, P, I, I64, I64, I64, I64, P, ctypes.c_float, P, I]),
     ("h3s_attention_causal", I, [P, P, P, P, I, I64, I64, I64, I64, I64, I64, P]),
     ("h3s_int8_linear", I, [P, P, I, I64, I64, P, I64, P, I64, P, P, I, I]),
+    ("h3s_ipc_handle", I, [P, P, P]),
+    ("h3s_ipc_open", P, [P, P]),
+    ("h3s_ipc_close", I, [P, P]),
+    ("h3s_ulysses_push_qkv", I, [P, P, I64, I64, I64, I, I, I, P]),
+    ("h3s_ulysses_push_out", I, [P, P, I64, I64, I64, I, I, I, P]),
     ("h3s_sage_prepass", I, [P, P, P, I, I64, I64, I64, I64, P, P, P]),
     ("h3s_stream", P, [P]),
     ("h3s_selftest_wait_timeout", I, [P, U64]),
@@ -204,6 +209,31 @@ class Context:
                     out: int, out_dt: int, group: int) -> None:
         check(self._lib.h3s_int8_linear(self.handle, x, x_dt, M, K, w, N, wscale, n_wscale, bias, out, out_dt, group),
               "h3s_int8_linear")
+
+    def ipc_handle(self, ptr: int) -> bytes:
+        buf = ctypes.create_string_buffer(64)
+        check(self._lib.h3s_ipc_handle(self.handle, ptr, ctypes.cast(buf, ctypes.c_void_p)), "h3s_ipc_handle")
+        return buf.raw
+
+    def ipc_open(self, handle: bytes) -> int:
+        if len(handle) != 64:
+            raise H3Error("h3s_ipc_open: a handle is 64 bytes")
+        buf = ctypes.create_string_buffer(handle, 64)
+        p = self._lib.h3s_ipc_open(self.handle, ctypes.cast(buf, ctypes.c_void_p))
+        if not p:
+            raise H3Error(f"h3s_ipc_open: {last_error()}")
+        return p
+
+    def ipc_close(self, ptr: int) -> None:
+        check(self._lib.h3s_ipc_close(self.handle, ptr), "h3s_ipc_close")
+
+    def ulysses_push_qkv(self, shard: int, s: int, H: int, D: int, es: int, P: int, rank: int, dst: list[int]) -> None:
+        table = (ctypes.c_void_p * len(dst))(*dst)
+        check(self._lib.h3s_ulysses_push_qkv(self.handle, shard, s, H, D, es, P, rank, table), "h3s_ulysses_push_qkv")
+
+    def ulysses_push_out(self, out_heads: int, s: int, H: int, D: int, es: int, P: int, rank: int, dst: list[int]) -> None:
+        table = (ctypes.c_void_p * len(dst))(*dst)
+        check(self._lib.h3s_ulysses_push_out(self.handle, out_heads, s, H, D, es, P, rank, table), "h3s_ulysses_push_out")
 
     def attention_causal(self, q: int, k: int, v: int, dt: int, L: int, Hq: int, Hkv: int, D: int, qs: int, kvs: int,
                          out: int) -> None:

@@ -54,3 +54,101 @@ def head_slice(qkv: torch.Tensor, rank: int, P: int, H: int, D: int) -> torch.Te
     S = qkv.shape[0]
     h = H // P
     return qkv.view(S, 3, H, D)[:, :, rank * h:(rank + 1) * h, :].reshape(S, 3 * h * D)
+
+
+class _DeviceBuffer:
+    """A device allocation of the h3s context seen as a torch tensor (through __cuda_array_interface__; 2-byte types
+    as int16, viewed as the element type afterwards)."""
+
+    def __init__(self, ptr: int, shape: tuple[int, ...], es: int):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": "<i2" if es == 2 else "<f4", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def _as_tensor(ptr: int, shape: tuple[int, ...], dtype: torch.dtype, dev: torch.device) -> torch.Tensor:
+    es = torch.empty((), dtype=dtype).element_size()
+    return torch.as_tensor(_DeviceBuffer(ptr, shape, es), device=dev).view(dtype)
+
+
+class PeerExchange:
+    """The Ulysses all-to-alls as stores into the other ranks' memory (h3s_ulysses_push_qkv / _out over CUDA IPC),
+    for P ranks on one node (one process per GPU). The relayout and the transfer are one kernel per direction; the
+    ranks meet through a one-element all-reduce on the current stream before a push (nobody still reads the buffer
+    being overwritten) and after it (everything has arrived). Same layouts and results as seq_to_heads /
+    heads_to_seq; the receive buffers belong to this object and are reused by every call."""
+
+    def __init__(self, s: int, H: int, D: int, dtype: torch.dtype = torch.float16, group=None):
+        from .native import dt_code  # noqa: F401  (the library must load: no exchange without it)
+        from .ops import context
+
+        self.group = group
+        self.P = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if H % self.P or self.P > 8:
+            raise ValueError(f"{H} heads over {self.P} ranks: H must be a multiple of the ranks, at most 8 ranks")
+        self.s, self.H, self.D, self.dtype = s, H, D, dtype
+        self.h = H // self.P
+        self.es = torch.empty((), dtype=dtype).element_size()
+        self.ctx = context()
+        dev = torch.device("cuda", torch.cuda.current_device())
+        S = self.P * s
+        self._own = [self.ctx.alloc(S * 3 * self.h * D * self.es), self.ctx.alloc(s * H * D * self.es)]
+        self.heads = _as_tensor(self._own[0], (S, 3 * self.h * D), dtype, dev)
+        self.out = _as_tensor(self._own[1], (s, H * D), dtype, dev)
+        # every rank's two buffers: handles gathered over the group, opened where they are another rank's
+        mine = torch.frombuffer(bytearray(self.ctx.ipc_handle(self._own[0]) + self.ctx.ipc_handle(self._own[1])),
+                                dtype=torch.uint8).to(dev)
+        every = [torch.empty_like(mine) for _ in range(self.P)]
+        dist.all_gather(every, mine, group=group)
+        self._opened = []
+        self.dst_heads, self.dst_out = [], []
+        for p, t in enumerate(every):
+            if p == self.rank:
+                self.dst_heads.append(self._own[0])
+                self.dst_out.append(self._own[1])
+                continue
+            raw = bytes(t.cpu().numpy().tobytes())
+            a, b = self.ctx.ipc_open(raw[:64]), self.ctx.ipc_open(raw[64:])
+            self._opened += [a, b]
+            self.dst_heads.append(a)
+            self.dst_out.append(b)
+        self._flag = torch.zeros(1, device=dev)
+        self._meet()
+
+    def _meet(self) -> None:
+        dist.all_reduce(self._flag, group=self.group)
+
+    def seq_to_heads(self, shard: torch.Tensor) -> torch.Tensor:
+        """Token-sharded qkv [s, 3*H*D] -> this rank's head-sharded qkv [S, 3*(H/P)*D] (token order)."""
+        if shard.shape != (self.s, 3 * self.H * self.D) or shard.dtype != self.dtype or not shard.is_contiguous():
+            raise ValueError(f"shard {list(shard.shape)} {shard.dtype}: [{self.s}, {3 * self.H * self.D}] "
+                             f"{self.dtype} contiguous expected")
+        self._meet()
+        self.ctx.ulysses_push_qkv(shard.data_ptr(), self.s, self.H, self.D, self.es, self.P, self.rank, self.dst_heads)
+        self._meet()
+        return self.heads
+
+    def heads_to_seq(self, out_heads: torch.Tensor) -> torch.Tensor:
+        """Head-sharded output [S, (H/P)*D] -> this rank's token-sharded output [S/P, H*D]."""
+        if out_heads.shape != (self.P * self.s, self.h * self.D) or out_heads.dtype != self.dtype or \
+                not out_heads.is_contiguous():
+            raise ValueError(f"output {list(out_heads.shape)}: [{self.P * self.s}, {self.h * self.D}] expected")
+        self._meet()
+        self.ctx.ulysses_push_out(out_heads.data_ptr(), self.s, self.H, self.D, self.es, self.P, self.rank,
+                                  self.dst_out)
+        self._meet()
+        return self.out
+
+    def close(self) -> None:
+        """Unmaps the other ranks' buffers and frees this rank's (after every rank is done with them)."""
+        torch.cuda.synchronize()
+        self._meet()
+        torch.cuda.synchronize()
+        for p in self._opened:
+            self.ctx.ipc_close(p)
+        self._opened = []
+        self._meet()
+        torch.cuda.synchronize()
+        for p in self._own:
+            self.ctx.free(p)
+        self._own = []

@@ -1,0 +1,69 @@
+"""The Ulysses exchange over peer memory (h3s_ulysses_push_qkv / _out through CUDA IPC) on 2 and 4 GPUs of one node:
+the same bits as the token <-> head re-sharding it replaces (ulysses.head_slice, and the inverse), for half,
+bfloat16 and float32 rows, with 16-byte vectors and with element copies (a head of 12 features is 24 bytes).
+Skipped with fewer GPUs than ranks (the round-end single-GPU run)."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        import datetime
+
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", rank))
+        from sycl_minimax_h3_b200 import ulysses
+
+        for S, H, D, dtype in ((1024, 8, 128, torch.float16), (512, 8, 12, torch.bfloat16), (256, 4, 64, torch.float32),
+                               (4096 * world, 32, 128, torch.float16)):
+            g = torch.Generator().manual_seed(S + H + D)
+            full = torch.randn(S, 3 * H * D, generator=g).to(dtype).cuda()     # every rank makes the same input
+            s = S // world
+            ex = ulysses.PeerExchange(s, H, D, dtype)
+            for step in range(2):                                               # the buffers are reused
+                shard = (full[rank * s:(rank + 1) * s] + step).contiguous()
+                heads = ex.seq_to_heads(shard)
+                want = ulysses.head_slice(full + step, rank, world, H, D)
+                assert torch.equal(heads.view(torch.int16 if dtype != torch.float32 else torch.int32),
+                                   want.view(torch.int16 if dtype != torch.float32 else torch.int32)), "forward"
+                h = H // world
+                out_heads = heads[:, 2 * h * D:].contiguous()                   # v of this rank's heads, all tokens
+                back = ex.heads_to_seq(out_heads)
+                want_b = (full + step)[rank * s:(rank + 1) * s, 2 * H * D:]
+                assert torch.equal(back.float(), want_b.float()), "inverse"
+            ex.close()
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception as e:  # reported to the parent
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_peer_exchange(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in ps)
+    for p in ps:
+        p.join(timeout=60)
+    assert all(v == "ok" for v in res.values()), res
