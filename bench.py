@@ -641,8 +641,10 @@ def vae_leg(dev, max_over_ranks, barrier, B=4, S=1797, H=32, D=64) -> dict:
 
 def ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier) -> dict:
     """c4: token-sharded qkv -> all-to-all -> attention of H/P heads over all S tokens -> inverse all-to-all. The
-    exchange is ulysses.PeerExchange (each rank stores its data straight into the other ranks' buffers over NVLink,
-    relayout included); NCCL's all_to_all_single with the relayout copies around it is timed beside it."""
+    exchange is ulysses.PeerExchange: the forward one push kernel that stores each rank's data straight into the
+    other ranks' buffers over NVLink (relayout included), the inverse inside the attention's epilogue (each output
+    row stored into its rank's token shard). NCCL's all_to_all_single with the relayout copies around it is timed
+    beside it."""
     import torch
 
     from sycl_minimax_h3_b200 import ops, ulysses
@@ -660,10 +662,14 @@ def ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier) -> dict:
         ev[0].record()
         qkv_heads = ex.seq_to_heads(shard) if peer else ulysses.seq_to_heads(shard, H, D)
         ev[1].record()
-        q, k, v = ops.Rows.qkv(qkv_heads, h, D)
-        ops.attention(q, k, v, out)
-        ev[2].record()
-        res = ex.heads_to_seq(out) if peer else ulysses.heads_to_seq(out, H, D)
+        if peer:   # the attention stores its output rows straight into every rank's token shard
+            res = ex.attention_to_seq(qkv_heads)
+            ev[2].record()
+        else:
+            q, k, v = ops.Rows.qkv(qkv_heads, h, D)
+            ops.attention(q, k, v, out)
+            ev[2].record()
+            res = ulysses.heads_to_seq(out, H, D)
         ev[3].record()
         if times is not None:
             times.append(ev)
@@ -688,7 +694,8 @@ def ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier) -> dict:
     tot, a2a, att = measure(True)
     tot_n, a2a_n, _ = measure(False)
     ex.close()
-    return {"tokens_per_gpu": s, "heads_per_gpu": h, "exchange": "peer stores over NVLink (CUDA IPC)",
+    return {"tokens_per_gpu": s, "heads_per_gpu": h,
+            "exchange": "peer stores over NVLink (CUDA IPC); the inverse in the attention epilogue",
             "ms_per_call": tot, "ms_all_to_all_exposed": a2a, "ms_attention": att,
             "tops": ops_per_call(S, H, D) / (tot / 1e3) / 1e12,
             "nccl_all_to_all": {"ms_per_call": tot_n, "ms_all_to_all_exposed": a2a_n}}

@@ -160,6 +160,12 @@ int h3s_ulysses_push_qkv(void* ctx, const void* shard, int64_t s, int64_t H, int
                          void* const* dst);
 int h3s_ulysses_push_out(void* ctx, const void* out_heads, int64_t s, int64_t H, int64_t D, int es, int P, int rank,
                          void* const* dst);
+/* h3s_attention of this rank's H heads over all S tokens (q, k, v as for h3s_attention) with the inverse exchange in
+ * its epilogue: the output row of token t is stored straight into rank t / (S/P)'s token shard out_shards[t / (S/P)]
+ * [S/P, P*H*D] (out_dt; this rank's own buffer or one opened with h3s_ipc_open) at row t % (S/P), columns
+ * rank*H*D .. rank*H*D + H*D - 1. No separate output pass; the ranks must meet before another rank reads its shard. */
+int h3s_attention_ulysses(void* ctx, const void* q, const void* k, const void* v, int dt, int64_t S, int64_t H,
+                          int64_t D, int64_t stride, void* const* out_shards, int P, int rank, int out_dt);
 
 /* The Sage pre-pass alone (kernels/h3sycl.cpp:1733-1761 as a callable step, for parity checks and for callers that
  * keep int8 q/k): iq, ik int8 [H, S, D]; sc float [2*H*nb + H*D] = q scales [H, nb], k scales [H, nb], k's channel

@@ -41,6 +41,14 @@ int h3sage_attention_strided(void* stream, const int8_t* q, const int8_t* k, con
                              const float* qscale, const float* kscale, int block, int64_t S, int64_t H, int64_t D,
                              float scale, int* err, uint64_t wait_ns);
 
+/* h3sage_attention_strided with the output rows spread over the P ranks of a Ulysses group (P <= 8, S a multiple of
+ * P): the row of token s goes to out_peers[s / (S/P)] (that rank's token shard, in this or another GPU's memory,
+ * already offset to this rank's head columns) at row s % (S/P), each stored as the attention produces it. */
+int h3sage_attention_peers(void* stream, const int8_t* q, const int8_t* k, const void* v, int64_t v_tok, int64_t v_head,
+                           void* const* out_peers, int P, int out_dt, int64_t out_tok, int64_t out_head,
+                           const float* qscale, const float* kscale, int block, int64_t S, int64_t H, int64_t D,
+                           float scale, int* err, uint64_t wait_ns);
+
 /* Waits for the stream and reports, as -1 with h3sage_error(), a kernel wait of this plugin that gave up since the
  * last check (the reference reports such failures only through its queue's wait). */
 int h3sage_check(void* stream);

@@ -60,6 +60,11 @@ struct AttnArgs {
     int D;                      // head size, 64 or 128: the kernels run 128 wide, and a 64-wide head reads as zeros in
                                 // features 64-127 (TMA fills what lies outside the tensor with zeros), so those
                                 // features of Q.K^T add nothing and those of P.V come out 0 and are not stored
+    // Output rows spread over the ranks of a Ulysses group (out_rows > 0): token s goes to out_peer[s / out_rows], a
+    // rank's token shard in its own or another GPU's memory (base already at this rank's head columns), at row
+    // s % out_rows; out is then unused. out_rows = 0: every row to out.
+    int out_rows;
+    void* out_peer[8];
 };
 
 template <bool I8>
@@ -109,12 +114,12 @@ __device__ __forceinline__ void tma_rows(void* dst, const CUtensorMap* map, uint
 
 // 32 consecutive output features of one row (fp32 values already divided by the row sum), rounded to half, then to
 // out_dt (kernels/h3sycl.cpp:1769-1771), stored at out + e0 elements.
-__device__ __forceinline__ void store_out32(const AttnArgs& a, long long e0, const float (&val)[32]) {
+__device__ __forceinline__ void store_out32(const AttnArgs& a, void* out, long long e0, const float (&val)[32]) {
     __half hv[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) hv[i] = __float2half_rn(val[i]);
     if (a.out_dt == F16) {
-        __half* dst = reinterpret_cast<__half*>(a.out) + e0;
+        __half* dst = reinterpret_cast<__half*>(out) + e0;
         if (a.out_vec) {
 #pragma unroll
             for (int v = 0; v < 4; ++v) reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(hv)[v];
@@ -125,7 +130,7 @@ __device__ __forceinline__ void store_out32(const AttnArgs& a, long long e0, con
         __nv_bfloat16 bv[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) bv[i] = __float2bfloat16_rn(__half2float(hv[i]));
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) + e0;
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(out) + e0;
         if (a.out_vec) {
 #pragma unroll
             for (int v = 0; v < 4; ++v) reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(bv)[v];
@@ -136,7 +141,7 @@ __device__ __forceinline__ void store_out32(const AttnArgs& a, long long e0, con
         float fv[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) fv[i] = __half2float(hv[i]);
-        float* dst = reinterpret_cast<float*>(a.out) + e0;
+        float* dst = reinterpret_cast<float*>(out) + e0;
         if (a.out_vec) {
 #pragma unroll
             for (int v = 0; v < 8; ++v) reinterpret_cast<float4*>(dst)[v] = reinterpret_cast<const float4*>(fv)[v];
@@ -150,7 +155,14 @@ __device__ __forceinline__ void store_out32(const AttnArgs& a, long long e0, con
 // out + b*out_seq + qrow*out_tok + h*out_head. Warp-collective (TMEM loads): every lane calls it; rows past S
 // (live = false) load but do not store.
 __device__ __forceinline__ void store_out_row(const AttnArgs& a, int b, int h, int qrow, uint32_t o_taddr, float inv, bool live) {
-    const long long base = (long long) b * a.out_seq + (long long) qrow * a.out_tok + (long long) h * a.out_head;
+    void* out = a.out;
+    int row = qrow;
+    if (a.out_rows > 0 && live) {
+        const int p = qrow / a.out_rows;
+        row = qrow - p * a.out_rows;
+        out = a.out_peer[p & 7];
+    }
+    const long long base = (long long) b * a.out_seq + (long long) row * a.out_tok + (long long) h * a.out_head;
 #pragma unroll
     for (int c4 = 0; c4 < 4; ++c4) {
         if (c4 * 32 >= a.D) break;
@@ -161,7 +173,7 @@ __device__ __forceinline__ void store_out_row(const AttnArgs& a, int b, int h, i
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(o[i]) * inv;
-        store_out32(a, base + c4 * 32, v);
+        store_out32(a, out, base + c4 * 32, v);
     }
 }
 

@@ -69,6 +69,7 @@ struct Ctx {
     int sage_state = 0;                          // 0 not loaded yet, 1 ready, -1 unavailable
     decltype(&h3sage_attention) sage_fn = nullptr;
     decltype(&h3sage_attention_strided) sage_strided = nullptr;
+    decltype(&h3sage_attention_peers) sage_peers = nullptr;
     decltype(&h3sage_error) sage_err = nullptr;
     // scratch, grow-only
     int8_t* sq = nullptr; size_t sq_cap = 0;     // q, k as int8 [H, S, D]
@@ -175,6 +176,7 @@ bool sage_load(Ctx& c) {
     c.sage_fn = (decltype(c.sage_fn)) dlsym(h, "h3sage_attention");
     c.sage_err = (decltype(c.sage_err)) dlsym(h, "h3sage_error");
     c.sage_strided = (decltype(c.sage_strided)) dlsym(h, "h3sage_attention_strided");
+    c.sage_peers = (decltype(c.sage_peers)) dlsym(h, "h3sage_attention_peers");
     if (!c.sage_fn || !c.sage_err) {
         std::fprintf(stderr, "h3cuda: %s lacks h3sage_attention; attention stays on the fp16 SDPA kernel\n", path.c_str());
         return false;
@@ -308,9 +310,18 @@ __global__ void hsd_to_rows(const __half* src, int S, int H, int D, void* out, i
 }
 
 // ---- Form 0: SageAttention v1 (kernels/h3sycl.cpp:1704-1777). 1 = not a shape this path takes. ----------------------
+// Output rows spread over the ranks of a Ulysses group (h3s_attention_ulysses): P token shards, row stride tok
+// elements, each base already at this rank's head columns.
+struct OutPeers {
+    void* const* p;
+    int P;
+    int64_t tok;
+};
+
 int attention_sage(Ctx& c, const void* q, const void* k, const void* v, int dt, int64_t S, int64_t H, int64_t D,
-                   int64_t stride, void* out, int out_dt) {
+                   int64_t stride, void* out, int out_dt, const OutPeers* peers = nullptr) {
     if ((D != 64 && D != 128) || S > INT32_MAX / D / H) return 1;   // the plugin's bounds (kernels/sage.cpp:33-35)
+    if (peers && !c.sage_peers) return 1;
     const size_t n = (size_t) S * H * D;
     const int64_t nb = (S + kSageBlock - 1) / kSageBlock;
     int8_t* iq = c.grow(c.sq, c.sq_cap, n);
@@ -336,7 +347,14 @@ int attention_sage(Ctx& c, const void* q, const void* k, const void* v, int dt, 
     const float scale = 1.0f / std::sqrt((float) D);
     const float* qs = sc;
     const float* ks = sc + H * nb;
-    if (c.sage_strided) {
+    if (peers) {
+        if (c.sage_peers(&st, iq, ik, vp, v_tok, v_head, peers->p, peers->P, out_dt, peers->tok, D, qs, ks, kSageBlock, S,
+                         H, D, scale, c.err, c.wait_ns) != 0) {
+            g_err = c.sage_err();
+            return -2;
+        }
+        ph.mark();
+    } else if (c.sage_strided) {
         if (c.sage_strided(&st, iq, ik, vp, v_tok, v_head, out, out_dt, H * D, D, qs, ks, kSageBlock, S, H, D, scale, c.err,
                            c.wait_ns) != 0) {
             g_err = c.sage_err();
@@ -359,7 +377,7 @@ int attention_sage(Ctx& c, const void* q, const void* k, const void* v, int dt, 
 
 // ---- Form 1: fp16 SDPA over B sequences (kernels/h3sycl.cpp:1464-1674) ------------------------------------------------
 int attention_sdpa(Ctx& c, const void* q, const void* k, const void* v, int dt, int64_t B, int64_t S, int64_t H, int64_t D,
-                   int64_t stride, void* out, int out_dt) {
+                   int64_t stride, void* out, int out_dt, const OutPeers* peers = nullptr) {
     if (D != 64 && D != 128) { g_err = "attention: head size " + std::to_string(D) + " (64 or 128 on this build)"; return -1; }
     if (S > INT32_MAX / 2 || B * H > 65535) { g_err = "attention: sequence or head count out of range"; return -1; }
     Phases ph(c);
@@ -403,6 +421,15 @@ int attention_sdpa(Ctx& c, const void* q, const void* k, const void* v, int dt, 
     a.out_head = D;
     a.out_dt = out_dt;
     a.out_vec = aligned16(out) ? 1 : 0;
+    if (peers) {   // B = 1
+        a.out_rows = (int) (S / peers->P);
+        a.out_tok = peers->tok;
+        for (int p = 0; p < peers->P; ++p) {
+            a.out_peer[p] = peers->p[p];
+            if (!aligned16(peers->p[p])) a.out_vec = 0;
+        }
+        a.out = peers->p[0];
+    }
     a.q_order = a.k_order = a.v_order = order;
     a.err = c.err;
     a.wait_ns = c.wait_ns;
@@ -700,6 +727,39 @@ int h3s_attention_batch(void* ctx, const void* q, const void* k, const void* v, 
         if (rc != 0) return rc;
     }
     return 0;
+}
+
+// h3s_attention for the heads of one rank of a Ulysses group, with the output rows stored straight into the token
+// shards of every rank (include/h3cuda.h)
+int h3s_attention_ulysses(void* ctx, const void* q, const void* k, const void* v, int dt, int64_t S, int64_t H,
+                          int64_t D, int64_t stride, void* const* out_shards, int P, int rank, int out_dt) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    if (S <= 0 || H <= 0 || D <= 0) return 0;
+    if (stride < H * D) { g_err = "h3s_attention_ulysses: the row stride is shorter than a row"; return -1; }
+    if (!check_dt(dt) || !check_dt(out_dt)) { g_err = "h3s_attention_ulysses: unknown element type"; return -1; }
+    if (P < 1 || P > 8 || rank < 0 || rank >= P || S % P != 0 || !out_shards) {
+        g_err = "h3s_attention_ulysses: 1 to 8 ranks dividing the sequence, and a destination per rank";
+        return -1;
+    }
+    const size_t oe = out_dt == F32 ? 4 : 2;
+    void* bases[8];
+    for (int p = 0; p < P; ++p) {
+        if (!out_shards[p]) { g_err = "h3s_attention_ulysses: destination " + std::to_string(p) + " is null"; return -1; }
+        bases[p] = static_cast<char*>(out_shards[p]) + (size_t) rank * H * D * oe;
+    }
+    const OutPeers peers{bases, P, (int64_t) P * H * D};
+    DeviceGuard g(c.device);
+    if (c.sage_want && S >= c.sage_min_s && sage_load(c)) {
+        const int rc = attention_sage(c, q, k, v, dt, S, H, D, stride, nullptr, out_dt, &peers);
+        if (rc == 0) return 0;
+        if (rc == -1) return -1;
+        if (rc == -2) {
+            std::fprintf(stderr, "h3cuda: SageAttention failed (%s); attention stays on the fp16 SDPA kernel\n", g_err.c_str());
+            cudaStreamSynchronize(c.st);
+            c.sage_state = -1;
+        }
+    }
+    return attention_sdpa(c, q, k, v, dt, 1, S, H, D, stride, nullptr, out_dt, &peers);
 }
 
 // kernels/h3sycl.cpp:870-898: the reference's refusals (D <= 256, Hq a multiple of Hkv), the arithmetic in causal.cuh

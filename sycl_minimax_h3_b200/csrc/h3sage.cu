@@ -41,9 +41,11 @@ int* own_word() {
     return g_word[dev];
 }
 
+// out_peers (P entries, P <= 8, S a multiple of P): the output rows of token s go to out_peers[s / (S / P)] at row
+// s % (S / P) instead of to out (Ulysses groups; see h3sage_attention_peers)
 int run(cudaStream_t st, const int8_t* q, const int8_t* k, const void* v, int64_t v_tok, int64_t v_head, void* out,
         int out_dt, int64_t out_tok, int64_t out_head, const float* qscale, const float* kscale, int block, int64_t S,
-        int64_t H, int64_t D, float scale, int* err, uint64_t wait_ns) {
+        int64_t H, int64_t D, float scale, int* err, uint64_t wait_ns, void* const* out_peers = nullptr, int P = 0) {
     if (D != 64 && D != 128) return fail("h3sage: head size " + std::to_string(D) + " (64 or 128)");
     if (block <= 0 || block % 64 != 0) return fail("h3sage: the scale block must be a multiple of 64");
     if (S <= 0 || H <= 0 || S > INT32_MAX / D / H) return fail("h3sage: sequence out of range");
@@ -73,6 +75,15 @@ int run(cudaStream_t st, const int8_t* q, const int8_t* k, const void* v, int64_
     a.out_dt = out_dt;
     const int es = out_dt == 0 ? 4 : 2;
     a.out_vec = ((reinterpret_cast<uintptr_t>(out) & 15) == 0 && (out_tok * es) % 16 == 0 && (out_head * es) % 16 == 0) ? 1 : 0;
+    if (out_peers) {
+        if (P < 1 || P > 8 || S % P != 0) return fail("h3sage: 1 to 8 ranks dividing the sequence");
+        a.out_rows = (int) (S / P);
+        for (int p = 0; p < P; ++p) {
+            if (!out_peers[p]) return fail("h3sage: destination " + std::to_string(p) + " is null");
+            a.out_peer[p] = out_peers[p];
+            if (reinterpret_cast<uintptr_t>(out_peers[p]) & 15) a.out_vec = 0;
+        }
+    }
     a.q_order = 0;
     a.k_order = 0;
     a.v_order = v_order;
@@ -109,6 +120,16 @@ int h3sage_attention_strided(void* stream, const int8_t* q, const int8_t* k, con
     cudaStream_t st = stream ? *static_cast<cudaStream_t*>(stream) : nullptr;
     return run(st, q, k, v, v_tok, v_head, out, out_dt, out_tok, out_head, qscale, kscale, block, S, H, D, scale, err,
                wait_ns);
+}
+
+int h3sage_attention_peers(void* stream, const int8_t* q, const int8_t* k, const void* v, int64_t v_tok, int64_t v_head,
+                           void* const* out_peers, int P, int out_dt, int64_t out_tok, int64_t out_head,
+                           const float* qscale, const float* kscale, int block, int64_t S, int64_t H, int64_t D,
+                           float scale, int* err, uint64_t wait_ns) {
+    cudaStream_t st = stream ? *static_cast<cudaStream_t*>(stream) : nullptr;
+    if (!out_peers) return fail("h3sage: no destination table");
+    return run(st, q, k, v, v_tok, v_head, out_peers[0], out_dt, out_tok, out_head, qscale, kscale, block, S, H, D,
+               scale, err, wait_ns, out_peers, P);
 }
 
 int h3sage_check(void* stream) {

@@ -50,6 +50,7 @@ CUDA_SYMBOLS = [
     ("h3s_ipc_close", I, [P, P]),
     ("h3s_ulysses_push_qkv", I, [P, P, I64, I64, I64, I, I, I, P]),
     ("h3s_ulysses_push_out", I, [P, P, I64, I64, I64, I, I, I, P]),
+    ("h3s_attention_ulysses", I, [P, P, P, P, I, I64, I64, I64, I64, P, I, I, I]),
     ("h3s_sage_prepass", I, [P, P, P, I, I64, I64, I64, I64, P, P, P]),
     ("h3s_stream", P, [P]),
     ("h3s_selftest_wait_timeout", I, [P, U64]),
@@ -60,6 +61,8 @@ SAGE_SYMBOLS = [
     ("h3sage_error", ctypes.c_char_p, []),
     ("h3sage_attention", I, [P, P, P, P, P, P, P, I, I64, I64, I64, ctypes.c_float]),
     ("h3sage_attention_strided", I, [P, P, P, P, I64, I64, P, I, I64, I64, P, P, I, I64, I64, I64, ctypes.c_float, P, U64]),
+    ("h3sage_attention_peers", I, [P, P, P, P, I64, I64, P, I, I, I64, I64, P, P, I, I64, I64, I64, ctypes.c_float, P,
+                                   U64]),
     ("h3sage_check", I, [P]),
 ]
 
@@ -234,6 +237,12 @@ class Context:
     def ulysses_push_out(self, out_heads: int, s: int, H: int, D: int, es: int, P: int, rank: int, dst: list[int]) -> None:
         table = (ctypes.c_void_p * len(dst))(*dst)
         check(self._lib.h3s_ulysses_push_out(self.handle, out_heads, s, H, D, es, P, rank, table), "h3s_ulysses_push_out")
+
+    def attention_ulysses(self, q: int, k: int, v: int, dt: int, S: int, H: int, D: int, stride: int,
+                          out_shards: list[int], P: int, rank: int, out_dt: int) -> None:
+        table = (ctypes.c_void_p * len(out_shards))(*out_shards)
+        check(self._lib.h3s_attention_ulysses(self.handle, q, k, v, dt, S, H, D, stride, table, P, rank, out_dt),
+              "h3s_attention_ulysses")
 
     def attention_causal(self, q: int, k: int, v: int, dt: int, L: int, Hq: int, Hkv: int, D: int, qs: int, kvs: int,
                          out: int) -> None:

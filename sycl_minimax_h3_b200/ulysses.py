@@ -139,6 +139,21 @@ class PeerExchange:
         self._meet()
         return self.out
 
+    def attention_to_seq(self, heads: torch.Tensor) -> torch.Tensor:
+        """The attention of this rank's heads over all tokens (heads [S, 3*(H/P)*D], q | k | v, as seq_to_heads
+        returns it), with the inverse exchange in the attention's epilogue (h3s_attention_ulysses): each output row
+        is stored straight into its rank's token shard. Returns this rank's token-sharded output [S/P, H*D]."""
+        from .native import dt_code
+
+        S, h, D = self.P * self.s, self.h, self.D
+        if heads.shape != (S, 3 * h * D) or heads.dtype != self.dtype or not heads.is_contiguous():
+            raise ValueError(f"heads {list(heads.shape)}: [{S}, {3 * h * D}] {self.dtype} contiguous expected")
+        base, es = heads.data_ptr(), self.es
+        self.ctx.attention_ulysses(base, base + h * D * es, base + 2 * h * D * es, dt_code(self.dtype), S, h, D,
+                                   3 * h * D, self.dst_out, self.P, self.rank, dt_code(self.dtype))
+        self._meet()
+        return self.out
+
     def close(self) -> None:
         """Unmaps the other ranks' buffers and frees this rank's (after every rank is done with them)."""
         torch.cuda.synchronize()

@@ -1,4 +1,5 @@
-"""The Ulysses exchange over peer memory (h3s_ulysses_push_qkv / _out through CUDA IPC) on 2 and 4 GPUs of one node:
+"""The Ulysses exchange over peer memory (h3s_ulysses_push_qkv / _out through CUDA IPC) on 2 and 4 GPUs of one node,
+and the attention with the inverse exchange in its epilogue (h3s_attention_ulysses, both the Sage and the fp16 path):
 the same bits as the token <-> head re-sharding it replaces (ulysses.head_slice, and the inverse), for half,
 bfloat16 and float32 rows, with 16-byte vectors and with element copies (a head of 12 features is 24 bytes).
 Skipped with fewer GPUs than ranks (the round-end single-GPU run)."""
@@ -30,7 +31,8 @@ def _worker(rank, world, port, q):
         from sycl_minimax_h3_b200 import ulysses
 
         for S, H, D, dtype in ((1024, 8, 128, torch.float16), (512, 8, 12, torch.bfloat16), (256, 4, 64, torch.float32),
-                               (4096 * world, 32, 128, torch.float16)):
+                               (4096 * world, 32, 128, torch.float16), (8192 * world, 8, 128, torch.float16),
+                               (640 * world, 8, 64, torch.bfloat16)):
             g = torch.Generator().manual_seed(S + H + D)
             full = torch.randn(S, 3 * H * D, generator=g).to(dtype).cuda()     # every rank makes the same input
             s = S // world
@@ -46,6 +48,19 @@ def _worker(rank, world, port, q):
                 back = ex.heads_to_seq(out_heads)
                 want_b = (full + step)[rank * s:(rank + 1) * s, 2 * H * D:]
                 assert torch.equal(back.float(), want_b.float()), "inverse"
+            if D in (64, 128) and dtype != torch.float32:
+                # the attention with the exchange in its epilogue: the same bits as the attention on this rank's
+                # heads followed by the inverse push
+                from sycl_minimax_h3_b200 import ops
+
+                heads = ex.seq_to_heads(full[rank * s:(rank + 1) * s].contiguous())
+                h = H // world
+                out_heads = torch.empty(S, h * D, dtype=dtype, device="cuda")
+                q, k, v = ops.Rows.qkv(heads, h, D)
+                ops.attention(q, k, v, out_heads)
+                want = ex.heads_to_seq(out_heads).clone()
+                got = ex.attention_to_seq(heads)
+                assert torch.equal(got.view(torch.int16), want.view(torch.int16)), "attention with the exchange"
             ex.close()
         dist.destroy_process_group()
         q.put((rank, "ok"))
