@@ -95,24 +95,39 @@ class PeerExchange:
         self._own = [self.ctx.alloc(S * 3 * self.h * D * self.es), self.ctx.alloc(s * H * D * self.es)]
         self.heads = _as_tensor(self._own[0], (S, 3 * self.h * D), dtype, dev)
         self.out = _as_tensor(self._own[1], (s, H * D), dtype, dev)
-        # every rank's two buffers: handles gathered over the group, opened where they are another rank's
-        mine = torch.frombuffer(bytearray(self.ctx.ipc_handle(self._own[0]) + self.ctx.ipc_handle(self._own[1])),
-                                dtype=torch.uint8).to(dev)
-        every = [torch.empty_like(mine) for _ in range(self.P)]
-        dist.all_gather(every, mine, group=group)
+        # every rank's two buffers: handles gathered over the group, opened where they are another rank's. A failure
+        # on any rank is decided together (below), so that no rank is left waiting in a collective the others skip.
+        why = ""
+        try:
+            mine = bytes(self.ctx.ipc_handle(self._own[0]) + self.ctx.ipc_handle(self._own[1]))
+        except Exception as e:
+            why, mine = str(e), bytes(128)
+        mine_t = torch.frombuffer(bytearray(mine), dtype=torch.uint8).to(dev)
+        every = [torch.empty_like(mine_t) for _ in range(self.P)]
+        dist.all_gather(every, mine_t, group=group)
         self._opened = []
         self.dst_heads, self.dst_out = [], []
-        for p, t in enumerate(every):
-            if p == self.rank:
-                self.dst_heads.append(self._own[0])
-                self.dst_out.append(self._own[1])
-                continue
-            raw = bytes(t.cpu().numpy().tobytes())
-            a, b = self.ctx.ipc_open(raw[:64]), self.ctx.ipc_open(raw[64:])
-            self._opened += [a, b]
-            self.dst_heads.append(a)
-            self.dst_out.append(b)
+        try:
+            if why:
+                raise RuntimeError(why)
+            for p, t in enumerate(every):
+                if p == self.rank:
+                    self.dst_heads.append(self._own[0])
+                    self.dst_out.append(self._own[1])
+                    continue
+                raw = bytes(t.cpu().numpy().tobytes())
+                self._opened.append(self.ctx.ipc_open(raw[:64]))
+                self.dst_heads.append(self._opened[-1])
+                self._opened.append(self.ctx.ipc_open(raw[64:]))
+                self.dst_out.append(self._opened[-1])
+        except Exception as e:  # decided together below, so that every rank takes the same path
+            why = str(e)
         self._flag = torch.zeros(1, device=dev)
+        ok = torch.tensor([0.0 if why else 1.0], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if ok.item() < 1.0:
+            self.close()
+            raise RuntimeError(f"PeerExchange: a rank could not open the other ranks' buffers ({why or 'elsewhere'})")
         self._meet()
 
     def _meet(self) -> None:
