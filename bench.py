@@ -641,10 +641,10 @@ def vae_leg(dev, max_over_ranks, barrier, B=4, S=1797, H=32, D=64) -> dict:
 
 def ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier) -> dict:
     """c4: token-sharded qkv -> all-to-all -> attention of H/P heads over all S tokens -> inverse all-to-all. The
-    exchange is ulysses.PeerExchange: the forward one push kernel that stores each rank's data straight into the
-    other ranks' buffers over NVLink (relayout included), the inverse inside the attention's epilogue (each output
-    row stored into its rank's token shard). NCCL's all_to_all_single with the relayout copies around it is timed
-    beside it."""
+    exchange is ulysses.PeerExchange: one push kernel per direction that stores each rank's data straight into the
+    other ranks' buffers over NVLink (relayout included); with H3_C4_FUSED=1 the inverse runs inside the attention's
+    epilogue instead (each output row stored into its rank's token shard). NCCL's all_to_all_single with the relayout
+    copies around it is timed beside it."""
     import torch
 
     from sycl_minimax_h3_b200 import ops, ulysses
@@ -655,6 +655,9 @@ def ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier) -> dict:
     shard = torch.randn(s, 3 * H * D, generator=g, device=dev, dtype=torch.float16)
     h = H // world
     out = torch.empty(S, h * D, dtype=torch.float16, device=dev)
+    # H3_C4_FUSED=1: the inverse exchange inside the attention epilogue (h3s_attention_ulysses) instead of a push
+    # kernel after it
+    fused = os.environ.get("H3_C4_FUSED") == "1"
     try:
         ex = ulysses.PeerExchange(s, H, D, torch.float16)   # every rank gets the same outcome (decided collectively)
     except RuntimeError as e:
@@ -666,9 +669,14 @@ def ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier) -> dict:
         ev[0].record()
         qkv_heads = ex.seq_to_heads(shard) if peer else ulysses.seq_to_heads(shard, H, D)
         ev[1].record()
-        if peer:   # the attention stores its output rows straight into every rank's token shard
+        if peer and fused:   # the attention stores its output rows straight into every rank's token shard
             res = ex.attention_to_seq(qkv_heads)
             ev[2].record()
+        elif peer:
+            q, k, v = ops.Rows.qkv(qkv_heads, h, D)
+            ops.attention(q, k, v, out)
+            ev[2].record()
+            res = ex.heads_to_seq(out)
         else:
             q, k, v = ops.Rows.qkv(qkv_heads, h, D)
             ops.attention(q, k, v, out)
@@ -703,7 +711,8 @@ def ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier) -> dict:
     tot, a2a, att = measure(True)
     ex.close()
     return {"tokens_per_gpu": s, "heads_per_gpu": h,
-            "exchange": "peer stores over NVLink (CUDA IPC); the inverse in the attention epilogue",
+            "exchange": "peer stores over NVLink (CUDA IPC)" + ("; the inverse in the attention epilogue" if fused else
+                                                               "; one push kernel per direction"),
             "ms_per_call": tot, "ms_all_to_all_exposed": a2a, "ms_attention": att,
             "tops": ops_per_call(S, H, D) / (tot / 1e3) / 1e12,
             "nccl_all_to_all": {"ms_per_call": tot_n, "ms_all_to_all_exposed": a2a_n}}
