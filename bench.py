@@ -644,9 +644,9 @@ def vae_leg(dev, max_over_ranks, barrier, B=4, S=1797, H=32, D=64) -> dict:
 def ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier) -> dict:
     """c4: token-sharded qkv -> all-to-all -> attention of H/P heads over all S tokens -> inverse all-to-all. The
     exchange is ulysses.PeerExchange: one push kernel per direction that stores each rank's data straight into the
-    other ranks' buffers over NVLink (relayout included); with H3_C4_FUSED=1 the inverse runs inside the attention's
-    epilogue instead (each output row stored into its rank's token shard). NCCL's all_to_all_single with the relayout
-    copies around it is timed beside it."""
+    other ranks' buffers over NVLink (relayout included) for the forward, the inverse inside the attention's epilogue
+    (each output row stored into its rank's token shard; H3_C4_FUSED=0: a push kernel after the attention). NCCL's
+    all_to_all_single with the relayout copies around it is timed beside it."""
     import torch
 
     from sycl_minimax_h3_b200 import ops, ulysses
@@ -657,9 +657,9 @@ def ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier) -> dict:
     shard = torch.randn(s, 3 * H * D, generator=g, device=dev, dtype=torch.float16)
     h = H // world
     out = torch.empty(S, h * D, dtype=torch.float16, device=dev)
-    # H3_C4_FUSED=1: the inverse exchange inside the attention epilogue (h3s_attention_ulysses) instead of a push
-    # kernel after it
-    fused = os.environ.get("H3_C4_FUSED") == "1"
+    # the inverse exchange inside the attention epilogue (h3s_attention_ulysses); H3_C4_FUSED=0: a push kernel after
+    # the attention instead
+    fused = os.environ.get("H3_C4_FUSED", "1") != "0"
     try:
         ex = ulysses.PeerExchange(s, H, D, torch.float16)   # every rank gets the same outcome (decided collectively)
     except RuntimeError as e:

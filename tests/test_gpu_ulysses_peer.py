@@ -4,7 +4,9 @@ the same bits as the token <-> head re-sharding it replaces (ulysses.head_slice,
 bfloat16 and float32 rows, with 16-byte vectors and with element copies (a head of 12 features is 24 bytes).
 Skipped with fewer GPUs than ranks (the round-end single-GPU run)."""
 import os
+import queue
 import socket
+import time
 
 import pytest
 import torch
@@ -20,7 +22,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, report):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
         torch.cuda.set_device(rank)
@@ -63,9 +65,9 @@ def _worker(rank, world, port, q):
                 assert torch.equal(got.view(torch.int16), want.view(torch.int16)), "attention with the exchange"
             ex.close()
         dist.destroy_process_group()
-        q.put((rank, "ok"))
+        report.put((rank, "ok"))
     except Exception as e:  # reported to the parent
-        q.put((rank, repr(e)))
+        report.put((rank, repr(e)))
 
 
 @pytest.mark.parametrize("world", [2, 4])
@@ -73,12 +75,22 @@ def test_peer_exchange(world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
-    q = ctx.Queue()
+    report = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, report)) for r in range(world)]
     for p in ps:
         p.start()
-    res = dict(q.get(timeout=300) for _ in ps)
+    res = {}
+    deadline = time.monotonic() + 300
+    while len(res) < world and time.monotonic() < deadline:
+        try:
+            r, v = report.get(timeout=5)
+            res[r] = v
+        except queue.Empty:
+            # a worker that ended without reporting fails the test now, not at the deadline
+            dead = [i for i, p in enumerate(ps) if p.exitcode is not None and i not in res]
+            if dead:
+                break
     for p in ps:
         p.join(timeout=60)
-    assert all(v == "ok" for v in res.values()), res
+    assert len(res) == world and all(v == "ok" for v in res.values()), res
