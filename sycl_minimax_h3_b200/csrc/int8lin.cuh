@@ -115,10 +115,12 @@ __device__ __forceinline__ int rq_code(float v, float inv, float scale) {
     return __float_as_int(t) - 0x4B400000;
 }
 
-// 16 values -> their 16 int8 codes, 4 per word (rq_code's arithmetic, checked once per chunk): with |y| <= 127 (the
-// row scale bounds every value), the rounded integer sits in the low byte of t = y + 1.5 * 2^23, whose bit pattern is
-// 0x4B400000 plus the integer; one predicate collects the values near a half (and any NaN or infinity, whose
-// difference is NaN), and such a chunk takes rq_code for every value.
+// 16 values -> their 16 int8 codes, 4 per word (rq_code's decision, checked once per chunk): with |v * inv| <= 127
+// (the row scale bounds every value), the integer nearest the exact product v * inv sits in the low byte of
+// t = 1.5 * 2^23 + v * inv (one rounding), whose bit pattern is 0x4B400000 plus the integer. That integer is rint of the
+// rounded quotient v / scale unless the product lies within 2^-14 of a half (the quotient and the product differ by
+// less than 1.2e-5 there); one predicate collects those values (and any NaN or infinity, whose difference is NaN), and
+// such a chunk takes rq_code for every value.
 __device__ __forceinline__ uint4 rq_codes16(const float (&v)[16], float inv, float scale) {
     uint32_t w[4];
     bool near = false;
@@ -127,9 +129,10 @@ __device__ __forceinline__ uint4 rq_codes16(const float (&v)[16], float inv, flo
         uint32_t tb[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-            const float y = __fmul_rn(v[4 * i + k], inv);
-            const float t = __fadd_rn(y, 12582912.0f);
-            const float d = __fsub_rn(y, __fsub_rn(t, 12582912.0f));
+            // t = 1.5*2^23 + v*inv rounded once: the integer nearest v*inv (half to even) in the low bits; d = v*inv
+            // minus that integer, rounded once
+            const float t = __fmaf_rn(v[4 * i + k], inv, 12582912.0f);
+            const float d = __fmaf_rn(v[4 * i + k], inv, -__fsub_rn(t, 12582912.0f));
             near |= !(fabsf(d) <= 0.5f - 6.103515625e-05f);
             tb[k] = __float_as_uint(t);
         }
@@ -191,7 +194,7 @@ __global__ void __launch_bounds__(kRqThreads) rotq_rows(const void* __restrict__
             }
             if constexpr (G <= 16) {
 #pragma unroll
-                for (int e = 0; e < 16; ++e) m = fmaxf(m, fabsf(v[e]));
+                for (int e = 0; e < 16; e += 2) m = fmax3(m, fabsf(v[e]), fabsf(v[e + 1]));
             }
             float4* s4 = reinterpret_cast<float4*>(base + rq_pad(16 * t));
 #pragma unroll
@@ -209,9 +212,10 @@ __global__ void __launch_bounds__(kRqThreads) rotq_rows(const void* __restrict__
 #pragma unroll
                     for (int j = 0; j < V; ++j) {
                         y[j] = __fmul_rn(y[j], RqDigits<G>::NORM);
-                        m = fmaxf(m, fabsf(y[j]));
                         lp[rq_line_off(j)] = y[j];
                     }
+#pragma unroll
+                    for (int j = 0; j < V; j += 2) m = fmax3(m, fabsf(y[j]), fabsf(y[j + 1]));
                 }
                 __syncthreads();
             }
@@ -294,7 +298,7 @@ __global__ void __launch_bounds__(kRqThreads) rotq_fast(const void* __restrict__
             }
             if constexpr (G <= 16) {
 #pragma unroll
-                for (int e = 0; e < 16; ++e) m = fmaxf(m, fabsf(v[e]));
+                for (int e = 0; e < 16; e += 2) m = fmax3(m, fabsf(v[e]), fabsf(v[e + 1]));
             }
             float4* s4 = reinterpret_cast<float4*>(sv + w * kRqWinPad + rq_pad(16 * t));
 #pragma unroll
@@ -316,9 +320,10 @@ __global__ void __launch_bounds__(kRqThreads) rotq_fast(const void* __restrict__
 #pragma unroll
                     for (int j = 0; j < V; ++j) {
                         y[j] = __fmul_rn(y[j], RqDigits<G>::NORM);
-                        m = fmaxf(m, fabsf(y[j]));
                         lp[rq_line_off(j)] = y[j];
                     }
+#pragma unroll
+                    for (int j = 0; j < V; j += 2) m = fmax3(m, fabsf(y[j]), fabsf(y[j + 1]));
                 }
             }
         }
