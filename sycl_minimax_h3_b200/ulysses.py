@@ -78,8 +78,7 @@ class PeerExchange:
     heads_to_seq; the receive buffers belong to this object and are reused by every call."""
 
     def __init__(self, s: int, H: int, D: int, dtype: torch.dtype = torch.float16, group=None):
-        from .native import dt_code  # noqa: F401  (the library must load: no exchange without it)
-        from .ops import context
+        from .ops import context   # loads libh3cuda.so: no exchange without it
 
         self.group = group
         self.P = dist.get_world_size(group)
