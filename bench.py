@@ -90,6 +90,16 @@ class Clocks:
                 "reasons": reasons, "samples": len(sm)}
 
 
+def bench_config(S: int, H: int, D: int, world: int, blocks: int) -> dict:
+    """The workload both arms name (the same keys and values, so that the lines compare)."""
+    return {"workload": (f"c3: {H} heads x {S:,} tokens x {D} per call" if (S, H) == (47232, 32) else
+                         f"profiling case: {H} heads x {S:,} tokens x {D} per call") +
+                        ", Sage path, fp16 q/k/v inside a qkv buffer (row stride 3*H*D), fp16 out; fresh blocks",
+            "S": S, "H": H, "D": D, "blocks": blocks,
+            "parallelism": f"heads/{world}" if world > 1 else "1 GPU",
+            "l2": "inputs larger than L2 (1.16 GB per block), a different block every step"}
+
+
 # ---------------------------------------------------------------------------------------------------------------------
 # CPU side: the oracle (the reference's attention restated; oracle/sage_ref.cpp)
 # ---------------------------------------------------------------------------------------------------------------------
@@ -133,7 +143,8 @@ class CpuSage:
         return {"value": ops_per_call(S, H, D) / t_call / 1e12, "unit": UNIT, "cores": self.o.threads(), "kind": "port",
                 "sample": f"S={S}, H={H}: whole pre-pass ({self.t_pre:.2f} s) + {done} of {H * S} query rows "
                           f"({t_rows:.2f} s), scaled to a whole call = {t_call:.1f} s",
-                "s_per_call": t_call}
+                "s_per_call": t_call, "measured": {"prepass_s": self.t_pre, "rows": done, "rows_s": t_rows,
+                                                   "rows_total": H * S, "ops_per_row": 4.0 * S * D}}
 
 
 def run_reference(args) -> None:
@@ -149,16 +160,27 @@ def run_reference(args) -> None:
         if i >= args.warmup:
             per_step.append(r)
     tops = statistics.median(r["value"] for r in per_step)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rows = sum(r["measured"]["rows"] for r in per_step)
+    rows_s = sum(r["measured"]["rows_s"] for r in per_step)
     line = {
         "impl": "reference", "metric": METRIC, "value": tops, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * statistics.median(r["s_per_call"] for r in per_step),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8+fp16", "data": DATA,
-        "config": {"workload": "c3: 32 heads x 47,232 tokens x 128, Sage path, fp16 in/out", "S": S, "H": H, "D": D},
+        "config": bench_config(S, H, D, world, min(50, args.warmup + args.steps)),
         "cpu_baseline": {k: per_step[-1][k] for k in ("value", "unit", "cores", "kind", "sample")},
         "e2e": {"value": tops, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        # what was timed, so that the value can be recomputed from this line: per step, a sample of query rows of one
+        # call (rows_s seconds for `rows` rows, each 4*S*D ops) plus the whole pre-pass once (prepass_s)
+        "measured": {"prepass_s": cpu.t_pre, "rows_timed": rows, "rows_s": rows_s, "rows_per_call": H * S,
+                     "ops_per_row": 4.0 * S * D, "steps_timed": len(per_step),
+                     "call_s": cpu.t_pre + rows_s / rows * H * S,
+                     "recompute": "value = 4*S^2*D*H / (prepass_s + rows_s / rows_timed * rows_per_call) / 1e12 (the "
+                                  "median over steps differs from this pooled form by the steps' spread)"},
         "note": "the reference's own attention (SYCL + oneDNN + un-vendored ARK) cannot be built or run here; this is "
-                "its algorithm restated in C++ (oracle/sage_ref.cpp) on the host cores, every step a sample of query "
-                "rows of one 47,232-token call",
+                "its algorithm restated in C++ (oracle/sage_ref.cpp; its pre-pass is bit-exact with the reference's "
+                "own source) on the host cores, every step a sample of query rows of one 47,232-token call "
+                "extrapolated by the exact per-row work; ms_per_step is that extrapolated call time, not wall time",
     }
     line["cpu_baseline"]["value"] = tops
     print(json.dumps(line), flush=True)
@@ -439,12 +461,7 @@ def main() -> None:
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_call, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int8+fp16", "data": DATA,
-            "config": {"workload": (f"c3: {H} heads x {S:,} tokens x 128 per call" if (S, H) == (47232, 32) else
-                                    f"profiling case: {H} heads x {S:,} tokens x 128 per call") +
-                                   ", Sage path, fp16 q/k/v inside a qkv buffer (row stride 3*H*D), fp16 out; fresh blocks",
-                       "S": S, "H": H, "D": D, "blocks": min(nblocks, args.warmup + args.steps),
-                       "parallelism": f"heads/{world}" if world > 1 else "1 GPU",
-                       "l2": "inputs larger than L2 (1.16 GB per block), a different block every step"},
+            "config": bench_config(S, H, D, world, min(nblocks, args.warmup + args.steps)),
             "ms_per_call": ms_call, "pct_int8_peak_measured_x2": value / world / (2 * peaks["bf16_tflops"]),
             "roofline": roofline, "prepass": prepass, "e2e": e2e, "gpu_launches": launches_per_call * args.steps,
             "clocks": clk.summary(), "extra": extra,
@@ -666,13 +683,15 @@ def ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier) -> dict:
         ex = None
         why = str(e)
 
-    def step(peer, times=None):
+    def step(peer, times=None, local=False):
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
         ev[0].record()
         qkv_heads = ex.seq_to_heads(shard) if peer else ulysses.seq_to_heads(shard, H, D)
         ev[1].record()
         if peer and fused:   # the attention stores its output rows straight into every rank's token shard
-            res = ex.attention_to_seq(qkv_heads)
+            # local: the same kernel with every row stored into this rank's own buffer (timing only), so that the
+            # difference to the peer form is what the inverse exchange costs inside the attention
+            res = ex.attention_to_seq(qkv_heads, [ex.dst_out[rank]] * world if local else None)
             ev[2].record()
         elif peer:
             q, k, v = ops.Rows.qkv(qkv_heads, h, D)
@@ -689,17 +708,20 @@ def ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier) -> dict:
             times.append(ev)
         return res
 
-    def measure(peer):
+    def measure(peer, local=False):
         for _ in range(3):
-            step(peer)
+            step(peer, local=local)
         torch.cuda.synchronize()
         barrier()
         times = []
         n = 10
         for _ in range(n):
-            step(peer, times)
+            step(peer, times, local=local)
         torch.cuda.synchronize()
-        ops.context(dev).wait()
+        if peer:
+            ex.check()
+        else:
+            ops.context(dev).wait()
         a2a = sum(e[0].elapsed_time(e[1]) + e[2].elapsed_time(e[3]) for e in times) / n
         att = sum(e[1].elapsed_time(e[2]) for e in times) / n
         tot = sum(e[0].elapsed_time(e[3]) for e in times) / n
@@ -711,13 +733,21 @@ def ulysses_leg(dev, world, rank, S, H, D, max_over_ranks, barrier) -> dict:
                 "ms_per_call": tot_n, "ms_all_to_all_exposed": a2a_n, "ms_attention": att_n,
                 "tops": ops_per_call(S, H, D) / (tot_n / 1e3) / 1e12}
     tot, a2a, att = measure(True)
+    res = {"tokens_per_gpu": s, "heads_per_gpu": h,
+           "exchange": "peer stores over NVLink (CUDA IPC)" + ("; the inverse in the attention epilogue" if fused else
+                                                              "; one push kernel per direction"),
+           "ms_per_call": tot, "ms_all_to_all_exposed": a2a, "ms_attention": att,
+           "tops": ops_per_call(S, H, D) / (tot / 1e3) / 1e12,
+           "nccl_all_to_all": {"ms_per_call": tot_n, "ms_all_to_all_exposed": a2a_n}}
+    if fused:
+        # the same attention with every output row stored locally: ms_attention minus this is the inverse exchange's
+        # own cost inside the epilogue (its NVLink stores and the two meetings around the kernel are in both)
+        _, _, att_local = measure(True, local=True)
+        res["ms_attention_local_stores"] = att_local
+        res["ms_inverse_exchange_in_epilogue"] = att - att_local
+        res["ms_exchange_total"] = a2a + att - att_local
     ex.close()
-    return {"tokens_per_gpu": s, "heads_per_gpu": h,
-            "exchange": "peer stores over NVLink (CUDA IPC)" + ("; the inverse in the attention epilogue" if fused else
-                                                               "; one push kernel per direction"),
-            "ms_per_call": tot, "ms_all_to_all_exposed": a2a, "ms_attention": att,
-            "tops": ops_per_call(S, H, D) / (tot / 1e3) / 1e12,
-            "nccl_all_to_all": {"ms_per_call": tot_n, "ms_all_to_all_exposed": a2a_n}}
+    return res
 
 
 if __name__ == "__main__":

@@ -23,8 +23,8 @@ extern "C" {
 /* The reason of the last failure of this library (kernels/sage.cpp:28). Process-wide, like the reference's. */
 const char* h3sage_error(void);
 
-/* 0 on success, else -1 with the reason in h3sage_error(). D must be 128 (the reference also takes 64:
- * kernels/sage.cpp:33); block a multiple of 64 (kernels/sage.cpp:34); S * H * D < 2^31 (kernels/sage.cpp:35).
+/* 0 on success, else -1 with the reason in h3sage_error(). D must be 64 or 128 (kernels/sage.cpp:33); block a
+ * multiple of 64 (kernels/sage.cpp:34); S * H * D < 2^31 (kernels/sage.cpp:35).
  * (kernels/sage.cpp:31-32) */
 int h3sage_attention(void* stream, const int8_t* q, const int8_t* k, const void* v, void* out, const float* qscale,
                      const float* kscale, int block, int64_t S, int64_t H, int64_t D, float scale);

@@ -24,8 +24,16 @@ _lib = None
 
 
 def build() -> str:
-    """Compiles liborc.so with oracle/Makefile (a no-op when it is current)."""
+    """Compiles liborc.so with oracle/Makefile (a no-op when it is current), and oracle/_ref/libref.so from the
+    reference's own source where that source is present (oracle/ref_build.py)."""
     subprocess.run(["make", "-s", "-C", HERE], check=True)
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("ref_build", os.path.join(HERE, "ref_build.py"))
+    rb = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(rb)
+    if rb.available():
+        rb.build()
     return LIB_PATH
 
 
@@ -255,3 +263,87 @@ def int8_linear_dense(x: np.ndarray, M: int, K: int, w: np.ndarray, N: int, wsca
     lib().orc_int8_linear_dense(_p(np.ascontiguousarray(x, np.float32)), M, K, _p(np.ascontiguousarray(w, np.int8)), N,
                                 _p(ws), ws.size, _p(b), group, _p(out))
     return out
+
+
+# ---- the reference's own source, compiled for the CPU (oracle/_ref/libref.so, built by oracle/ref_build.py) ---------
+# These run kernels/h3sycl.cpp:38-63, 1276-1376, 1733-1771 of the reference unchanged (through oracle/ref_shim.h), so
+# the restatement above and the GPU kernels can be compared with the reference itself. The library is built where the
+# reference's source is present and travels with the other built files; ref_available() is False without it.
+REF_LIB_PATH = os.path.join(HERE, "_ref", "libref.so")
+_ref = None
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_LIB_PATH)
+
+
+def ref_lib() -> ctypes.CDLL:
+    global _ref
+    if _ref is None:
+        if not ref_available():
+            raise FileNotFoundError(f"{REF_LIB_PATH} is missing: build it with oracle/ref_build.py where the "
+                                    "reference's source is present")
+        L = ctypes.CDLL(REF_LIB_PATH)
+        P, I64, I = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+        L.ref_load.argtypes = [P, I, ctypes.c_uint64]
+        L.ref_load.restype = ctypes.c_float
+        L.ref_store.argtypes = [P, I, ctypes.c_uint64, ctypes.c_float]
+        L.ref_store.restype = None
+        L.ref_sage_prepass.argtypes = [P, P, P, I, I64, I64, I64, I64, P, P, P, P]
+        L.ref_sage_prepass.restype = None
+        L.ref_out_relayout.argtypes = [P, P, I, I64, I64, I64]
+        L.ref_out_relayout.restype = None
+        L.ref_rms_rope.argtypes = [P, I, I64, I64, I64, I64, P, ctypes.c_float, P, I]
+        L.ref_rms_rope.restype = I
+        L.ref_error.restype = ctypes.c_char_p
+        _ref = L
+    return _ref
+
+
+def ref_sage_prepass(q, k, v, dt: int, S: int, H: int, D: int, stride: int):
+    """The reference's pre-pass (kernels/h3sycl.cpp:1733-1764) as compiled from its source: same returns as
+    sage_prepass (iq, ik, qs, ks, kmean, hv)."""
+    nb = (S + BLOCK - 1) // BLOCK
+    iq = np.empty((H, S, D), np.int8)
+    ik = np.empty((H, S, D), np.int8)
+    sc = np.empty(2 * H * nb + H * D, np.float32)
+    hv = np.empty((H, S, D), np.uint16)
+    ref_lib().ref_sage_prepass(_p(q), _p(k), _p(v), dt, S, H, D, stride, _p(iq), _p(ik), _p(sc), _p(hv))
+    return iq, ik, sc[: H * nb].reshape(H, nb).copy(), sc[H * nb: 2 * H * nb].reshape(H, nb).copy(), \
+        sc[2 * H * nb:].copy(), hv
+
+
+def ref_out_relayout(ao_bits: np.ndarray, out_dt: int, S: int, H: int, D: int) -> np.ndarray:
+    """kernels/h3sycl.cpp:1769-1771 from the reference's source: half [H, S, D] -> out_dt [S, H*D] (bits)."""
+    out = np.empty((S, H * D), np.float32 if out_dt == F32 else np.uint16)
+    ref_lib().ref_out_relayout(_p(np.ascontiguousarray(ao_bits, np.uint16)), _p(out), out_dt, S, H, D)
+    return out
+
+
+def ref_load(x: np.ndarray, dt: int) -> np.ndarray:
+    """kernels/h3sycl.cpp:49-55 (load) from the reference's source, element by element."""
+    x = np.ascontiguousarray(x)
+    L = ref_lib()
+    return np.array([L.ref_load(_p(x), dt, i) for i in range(x.size)], np.float32)
+
+
+def ref_store(v: np.ndarray, dt: int) -> np.ndarray:
+    """kernels/h3sycl.cpp:56-62 (store) from the reference's source: float32 values -> element bits of type dt."""
+    v = np.ascontiguousarray(v, np.float32)
+    out = np.empty(v.shape, np.float32 if dt == F32 else np.uint16)
+    L = ref_lib()
+    for i in range(v.size):
+        L.ref_store(_p(out), dt, i, float(v.flat[i]))
+    return out
+
+
+def ref_rms_rope(x: np.ndarray, dt: int, M: int, H: int, D: int, stride: int, weight: np.ndarray, eps: float,
+                 cs: np.ndarray, rot_dim: int) -> np.ndarray:
+    """h3s_rms_rope (kernels/h3sycl.cpp:1276-1376) from the reference's source on a copy of x (its rsqrt correctly
+    rounded: SYCL leaves rsqrt's accuracy to the implementation)."""
+    y = np.array(x, copy=True)
+    rc = ref_lib().ref_rms_rope(_p(y), dt, M, H, D, stride, _p(np.ascontiguousarray(weight, np.float32)),
+                                ctypes.c_float(eps), _p(np.ascontiguousarray(cs, np.float32)), rot_dim)
+    if rc != 0:
+        raise ValueError(ref_lib().ref_error().decode())
+    return y

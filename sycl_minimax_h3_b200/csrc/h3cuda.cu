@@ -6,8 +6,8 @@
 //   dispatcher          kernels/h3sycl.cpp:1779-1816: Sage when S >= sage_min_s and libh3sage.so loads, else fp16 SDPA
 //   Sage pre-pass       kernels/h3sycl.cpp:1704-1764: K channel mean || Q quantiser, then K quantiser (prepass.cuh)
 //   plugin loader       kernels/h3sycl.cpp:1683-1701: dlopen libh3sage.so from this library's directory
-//   fp16 SDPA           kernels/h3sycl.cpp:1464-1674 (oneDNN's fused graph): attn_fwd<false> (attn.cuh), reading q, k,
-//                       v in place through TMA and writing the token-major output directly (no relayout copies)
+//   fp16 SDPA           kernels/h3sycl.cpp:1464-1674 (oneDNN's fused graph): attn_sage3<false> (attn3.cuh), reading
+//                       q, k, v in place through TMA and writing the token-major output directly (no relayout copies)
 //
 // There is no CPU path and no score-table ("split") form: every attention call runs the tcgen05 kernels, or fails.
 #include <cuda_runtime.h>
@@ -114,6 +114,12 @@ int cuda_fail(const char* what, cudaError_t e) {
     return -1;
 }
 
+// The limit of every wait inside a kernel: H3S_WAIT_MS milliseconds, 2 s by default.
+uint64_t env_wait_ns() {
+    if (const char* e = std::getenv("H3S_WAIT_MS")) return (uint64_t) std::max(1, std::atoi(e)) * 1000000ull;
+    return 2000000000ull;
+}
+
 // what every way of making a context shares (kernels/h3sycl.cpp:216-235)
 bool init(Ctx& c) {
     cudaDeviceProp p{};
@@ -127,7 +133,7 @@ bool init(Ctx& c) {
     c.poison = std::getenv("H3S_POISON") != nullptr;
     if (const char* e = std::getenv("H3S_ATTN")) c.sage_want = std::strcmp(e, "onednn") != 0 && std::strcmp(e, "sdpa") != 0;
     if (const char* e = std::getenv("H3S_SAGE_MIN_S")) c.sage_min_s = std::max<int64_t>(0, std::atoll(e));
-    if (const char* e = std::getenv("H3S_WAIT_MS")) c.wait_ns = (uint64_t) std::max(1, std::atoi(e)) * 1000000ull;
+    c.wait_ns = env_wait_ns();
     cudaError_t e;
     if ((e = cudaStreamCreateWithFlags(&c.aux, cudaStreamNonBlocking)) != cudaSuccess ||
         (e = cudaEventCreateWithFlags(&c.ev_fork, cudaEventDisableTiming)) != cudaSuccess ||
@@ -1016,7 +1022,7 @@ int h3s_attention_sage_static(void* stream, const void* q, const void* k, const 
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
     }
-    const uint64_t wait_ns = 2000000000ull;
+    const uint64_t wait_ns = env_wait_ns();
     if (tma) {
         using M = MeanCfg<F16>;
         if ((e = cudaFuncSetAttribute(kmean_tma<F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, M::SMEM)) != cudaSuccess)

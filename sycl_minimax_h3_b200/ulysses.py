@@ -153,20 +153,46 @@ class PeerExchange:
         self._meet()
         return self.out
 
-    def attention_to_seq(self, heads: torch.Tensor) -> torch.Tensor:
+    def attention_to_seq(self, heads: torch.Tensor, dst: list[int] | None = None) -> torch.Tensor:
         """The attention of this rank's heads over all tokens (heads [S, 3*(H/P)*D], q | k | v, as seq_to_heads
         returns it), with the inverse exchange in the attention's epilogue (h3s_attention_ulysses): each output row
-        is stored straight into its rank's token shard. Returns this rank's token-sharded output [S/P, H*D]."""
+        is stored straight into its rank's token shard. Returns this rank's token-sharded output [S/P, H*D].
+
+        The ranks meet before the attention (no rank still reads its shard from the previous call) and after it
+        (every row has arrived). A wait that gives up inside the kernel is reported by check(), not here.
+        dst replaces the destination table (P device pointers); a table of this rank's own buffer P times keeps
+        every store local, which times the same kernel without the NVLink traffic."""
         from .native import dt_code
 
         S, h, D = self.P * self.s, self.h, self.D
         if heads.shape != (S, 3 * h * D) or heads.dtype != self.dtype or not heads.is_contiguous():
             raise ValueError(f"heads {list(heads.shape)}: [{S}, {3 * h * D}] {self.dtype} contiguous expected")
         base, es = heads.data_ptr(), self.es
+        # every rank has finished reading its token shard (self.out) of the previous call before any epilogue
+        # overwrites it
+        self._meet()
         self.ctx.attention_ulysses(base, base + h * D * es, base + 2 * h * D * es, dt_code(self.dtype), S, h, D,
-                                   3 * h * D, self.dst_out, self.P, self.rank, dt_code(self.dtype))
+                                   3 * h * D, dst if dst is not None else self.dst_out, self.P, self.rank,
+                                   dt_code(self.dtype))
         self._meet()
         return self.out
+
+    def check(self) -> None:
+        """Raises on every rank together when a kernel of any rank gave up on a wait since the last check.
+
+        A rank whose attention gave up sets only its own context's error word and skips its stores into the other
+        ranks' shards, which then hold stale rows with no error of their own. This waits for the rank's stream, reads
+        and clears its error word (h3s_wait), and takes the maximum over the group, so that no rank goes on with
+        rows another rank failed to write. Collective: every rank calls it at the same point."""
+        why = ""
+        try:
+            self.ctx.wait()
+        except Exception as e:  # decided together below
+            why = str(e)
+        bad = torch.tensor([1.0 if why else 0.0], device=self._flag.device)
+        dist.all_reduce(bad, op=dist.ReduceOp.MAX, group=self.group)
+        if bad.item() > 0:
+            raise RuntimeError(f"PeerExchange: a kernel gave up on a wait ({why or 'on another rank'})")
 
     def close(self) -> None:
         """Unmaps the other ranks' buffers and frees this rank's (after every rank is done with them)."""

@@ -51,11 +51,33 @@ def sample_rows(S: int, H: int, n: int | None, seed: int = 0):
     if n is None or n >= S * H:
         return np.repeat(np.arange(H), S), np.tile(np.arange(S), H)
     rng = np.random.default_rng(seed)
-    rh = rng.integers(0, H, n)
+    rh = rng.permutation(np.arange(n) % H)          # every head, when n >= H
     rs = rng.integers(0, S, n)
     rh[:2] = [0, H - 1]
     rs[:2] = [0, S - 1]
     return rh, rs
+
+
+def attention_stats(qkv_cpu: torch.Tensor, got: torch.Tensor, H: int, D: int, sage: bool, rows=None, dt=None) -> dict:
+    """The GPU output against float64 softmax of the same inputs and against the oracle's restatement of the same
+    arithmetic (Sage or SDPA semantics) on the chosen rows: min row cosine and max-abs error of each."""
+    S = qkv_cpu.shape[0]
+    host = bits(qkv_cpu)
+    if dt is None:
+        dt = {torch.float16: oracle.F16, torch.bfloat16: oracle.BF16, torch.float32: oracle.F32}[qkv_cpu.dtype]
+    st = 3 * H * D
+    rh, rs = rows if rows is not None else sample_rows(S, H, None)
+    exact = oracle.exact_rows(host, (host, H * D), (host, 2 * H * D), dt, S, H, D, st, rh, rs)
+    g = got.float().cpu().numpy().reshape(S, H, D)[rs, rh, :]
+    if sage:
+        iq, ik, qs, ks, km, hv = oracle.sage_prepass(host, (host, H * D), (host, 2 * H * D), dt, S, H, D, st)
+        same = half_bits_to_f32(oracle.sage_rows(iq, ik, hv, qs, ks, S, H, D, rh, rs))
+    else:
+        same = half_bits_to_f32(oracle.sdpa_rows(host, (host, H * D), (host, 2 * H * D), dt, S, H, D, st, rh, rs))
+    return {"rows": int(len(rh)), "min_cos_vs_exact": float(oracle.row_cosines(g, exact).min()),
+            "max_abs_vs_exact": float(np.max(np.abs(g - exact))),
+            "min_cos_vs_same_semantics": float(oracle.row_cosines(g, same).min()),
+            "max_abs_vs_same_semantics": float(np.max(np.abs(g - same)))}
 
 
 def check_attention(qkv_cpu: torch.Tensor, got: torch.Tensor, H: int, D: int, sage: bool, rows=None, dt=None):
@@ -100,5 +122,5 @@ def gpu_prepass(qkv: torch.Tensor, H: int, D: int, stride: int | None = None, dt
             s[2 * H * nb:])
 
 
-__all__ = ["make_qkv", "bits", "run_attention", "check_attention", "gpu_prepass", "sample_rows", "tok_rows_to_head_rows",
+__all__ = ["make_qkv", "bits", "run_attention", "check_attention", "attention_stats", "gpu_prepass", "sample_rows", "tok_rows_to_head_rows",
            "half_bits_to_f32", "MIN_ROW_COSINE", "MAX_ABS_VS_EXACT"]

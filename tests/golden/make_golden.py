@@ -5,7 +5,9 @@ Each fixture holds seeded inputs (q, k, v as the strided parts of one qkv buffer
 the reference's attention path makes of them, as restated by the oracle: the Sage pre-pass (int8 q and k, the q and k
 scales per 64-row block, k's channel mean; kernels/h3sycl.cpp:1733-1761) and the h3s_attention output through the Sage
 path and through the fp16 SDPA path (kernels/h3sycl.cpp:1779-1798). The reference has no fixture of its own for this
-path, so these pin the oracle against regressions and give the GPU tests exact expected int8 / scale bits.
+path, so these pin the oracle against regressions and give the GPU tests exact expected int8 / scale bits. Where the
+reference's source is present, its own pre-pass lines compiled for the CPU (oracle/_ref/libref.so) must give the same
+int8 q / k, scales and mean before a fixture is written (tests/test_ref_pin.py checks the committed ones against it).
 """
 from __future__ import annotations
 
@@ -43,6 +45,11 @@ def compute(orc, f) -> dict:
     qkv = np.ascontiguousarray(f["qkv"])
     st = 3 * H * D
     iq, ik, qs, ks, km, _ = orc.sage_prepass(qkv, (qkv, H * D), (qkv, 2 * H * D), dt, S, H, D, st)
+    if orc.ref_available():
+        ref = orc.ref_sage_prepass(qkv, (qkv, H * D), (qkv, 2 * H * D), dt, S, H, D, st)[:5]
+        for name, a, b in zip(("iq", "ik", "qs", "ks", "kmean"), (iq, ik, qs, ks, km), ref):
+            assert np.array_equal(np.asarray(a).view(np.uint8), np.asarray(b).view(np.uint8)), \
+                f"the oracle's {name} differs from the reference's own pre-pass"
     args = (qkv, (qkv, H * D), (qkv, 2 * H * D), dt, S, H, D, st)
     return {
         "iq": iq, "ik": ik, "qs": qs, "ks": ks, "kmean": km,

@@ -1,5 +1,6 @@
 """The Sage pre-pass on the GPU (K channel mean, int8 Q / K-mean quantiser) bit for bit against the oracle's
-restatement of kernels/h3sycl.cpp:1733-1761, through h3s_sage_prepass of the C ABI."""
+restatement of kernels/h3sycl.cpp:1733-1761, through h3s_sage_prepass of the C ABI, and against the reference's own
+pre-pass compiled from its source (oracle/_ref/libref.so) at configs[0], [2] and [3]."""
 import numpy as np
 import pytest
 import torch
@@ -65,3 +66,17 @@ def test_prepass_golden(cuda):
         assert np.array_equal(qs.view(np.uint32), f["qs"].view(np.uint32)), path
         assert np.array_equal(ks.view(np.uint32), f["ks"].view(np.uint32)), path
         assert np.array_equal(km.view(np.uint32), f["kmean"].view(np.uint32)), path
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="oracle/_ref/libref.so is not built")
+@pytest.mark.parametrize("S,H", [(2048, 8), (16848, 32), (47232, 32)])
+def test_prepass_vs_reference_source(S, H, cuda):
+    """configs[0], [2], [3] at full size: the GPU's int8 q / k, scales and K mean are the bits the reference's own
+    kernels/h3sycl.cpp:1733-1761 make of the same inputs (compiled for the CPU from its source)."""
+    D = 128
+    qkv = make_qkv(S, H, D, seed=S + 1)
+    got = gpu_prepass(qkv.to(cuda), H, D)
+    host = bits(qkv)
+    want = oracle.ref_sage_prepass(host, (host, H * D), (host, 2 * H * D), native.F16, S, H, D, 3 * H * D)[:5]
+    for name, g, w in zip(("iq", "ik", "qs", "ks", "kmean"), got, want):
+        assert np.array_equal(np.asarray(g).view(np.uint8), np.asarray(w).view(np.uint8)), f"{name} (S={S}, H={H})"

@@ -89,3 +89,28 @@ def test_refusals_and_degenerate_sizes(cuda):
     with pytest.raises(native.H3Error):
         x = torch.zeros(4, 128, dtype=torch.float16, device=cuda)
         ops.rms_rope(ops.Rows.packed(x, 1, 128), torch.ones(64, device=cuda), 1e-5, torch.zeros(4 * 128, device=cuda), 128)
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="oracle/_ref/libref.so is not built")
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("D,rot", [(128, 96), (128, 128), (64, 64), (100, 20)])
+def test_vs_reference_source(dtype, D, rot, cuda):
+    """The GPU kernel against h3s_rms_rope compiled from the reference's own source (its rsqrt correctly rounded)."""
+    for M, offset in ((257, 0), (64, 3)):
+        g = torch.Generator().manual_seed(M + D + rot)
+        H = 3
+        stride = 3 * H * D + offset
+        buf = (torch.randn(M * stride + offset, generator=g) * 3).to(dtype)
+        w = (1 + 0.2 * torch.randn(D, generator=g)).float()
+        ang = torch.rand(M, rot // 2, generator=g) * 14 - 7
+        cs = torch.stack([torch.cos(ang), torch.sin(ang)], -1).float().contiguous()
+        want = oracle.ref_rms_rope(np.ascontiguousarray(bits(buf)[offset:]), CODE[dtype], M, H, D, stride, w.numpy(),
+                                   1e-5, cs.numpy(), rot)
+        dev = buf.to(cuda)
+        ctx = ops.context(cuda)
+        wd, csd = w.to(cuda), cs.to(cuda)
+        ctx.rms_rope(dev.data_ptr() + offset * dev.element_size(), CODE[dtype], M, H, D, stride, wd.data_ptr(), 1e-5,
+                     csd.data_ptr(), rot)
+        ctx.wait()
+        got = bits(dev)[offset:]
+        assert np.array_equal(got, want), f"M={M}: {np.count_nonzero(got != want)} of {got.size} differ"

@@ -1,4 +1,4 @@
-"""The Ulysses exchange over peer memory (h3s_ulysses_push_qkv / _out through CUDA IPC) on 2 and 4 GPUs of one node,
+"""The Ulysses exchange over peer memory (h3s_ulysses_push_qkv / _out through CUDA IPC) on 2, 4 and 8 GPUs of one node,
 and the attention with the inverse exchange in its epilogue (h3s_attention_ulysses, both the Sage and the fp16 path):
 the same bits as the token <-> head re-sharding it replaces (ulysses.head_slice, and the inverse), for half,
 bfloat16 and float32 rows, with 16-byte vectors and with element copies (a head of 12 features is 24 bytes).
@@ -35,8 +35,12 @@ def _worker(rank, world, port, report):
         for S, H, D, dtype in ((1024, 8, 128, torch.float16), (512, 8, 12, torch.bfloat16), (256, 4, 64, torch.float32),
                                (4096 * world, 32, 128, torch.float16), (8192 * world, 8, 128, torch.float16),
                                (640 * world, 8, 64, torch.bfloat16)):
-            g = torch.Generator().manual_seed(S + H + D)
-            full = torch.randn(S, 3 * H * D, generator=g).to(dtype).cuda()     # every rank makes the same input
+            if H % world:
+                continue                                                        # fewer heads than ranks
+            g = torch.Generator(device="cuda")
+            g.manual_seed(S + H + D)
+            # every rank makes the same input (the same seeded generator on every GPU)
+            full = torch.randn(S, 3 * H * D, generator=g, device="cuda").to(dtype)
             s = S // world
             ex = ulysses.PeerExchange(s, H, D, dtype)
             for step in range(2):                                               # the buffers are reused
@@ -61,8 +65,17 @@ def _worker(rank, world, port, report):
                 q, k, v = ops.Rows.qkv(heads, h, D)
                 ops.attention(q, k, v, out_heads)
                 want = ex.heads_to_seq(out_heads).clone()
+                # NaN in every rank's shard first: each row the comparison sees must have been stored over CUDA IPC by
+                # the epilogue of the rank that owns its heads (attention_to_seq meets before any epilogue stores)
+                ex.out.fill_(float("nan"))
                 got = ex.attention_to_seq(heads)
+                ex.check()
                 assert torch.equal(got.view(torch.int16), want.view(torch.int16)), "attention with the exchange"
+                # twice in a row: the second call's stores wait for every rank to have read the first call's rows
+                first = got.clone()
+                again = ex.attention_to_seq(heads)
+                ex.check()
+                assert torch.equal(again.view(torch.int16), first.view(torch.int16)), "second attention"
             ex.close()
         dist.destroy_process_group()
         report.put((rank, "ok"))
@@ -70,7 +83,7 @@ def _worker(rank, world, port, report):
         report.put((rank, repr(e)))
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_peer_exchange(world):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
