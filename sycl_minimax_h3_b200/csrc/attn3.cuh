@@ -2,9 +2,10 @@
 // own S buffer, softmax warpgroup and O accumulator in TMEM; every key tile's scores are computed in two halves of 64
 // keys so that the next tile's scores are mostly ready before the softmax of this one ends.
 //
-// Warps: 0 TMA producer of Q0, Q1 (once) and the ring of int8 K tiles; 1 TMEM owner and MMA issuer (the whole warp runs
-// the loop, elect.sync picks the issuing lane); 2 TMA producer of the ring of half V tiles; 3 idle; 4-7 softmax of
-// query tile 0, 8-11 of tile 1 (one thread per query row; warp w reads TMEM lane quarter w % 4).
+// Warps: 0 TMA producer of Q0, Q1 (once) and the ring of K tiles; 1 TMEM owner and MMA issuer of query tile 0, 3 MMA
+// issuer of tile 1 (each whole warp runs its loop, elect.sync picks the issuing lane); 2 TMA producer of the ring of
+// half V tiles; 4-7 softmax of query tile 0, 8-11 of tile 1 (one thread per query row; warp w reads TMEM lane quarter
+// w % 4). The same kernel, instantiated with I8 = false, is the fp16 SDPA (fp16 Q.K^T, fp32 scores, one scale).
 // TMEM (512 columns): S0 0-127, S1 128-255, O0 256-383, O1 384-511. In S_t, columns 0-63 hold the scores of keys 0-63
 // of a key tile (S_lo) and then P_t of all 128 keys (half, two per column); columns 64-127 hold the scores of keys
 // 64-127 (S_hi).
@@ -29,9 +30,15 @@
 #pragma once
 #include <cstdlib>
 
-#include "attn2.cuh"
+#include "attn_common.cuh"
 
 namespace h3 {
+
+// The int32 bits that become -inf once the bias is added: keys past S.
+constexpr uint32_t kMaskedRaw = 0xFF800000u - kBias;
+
+// Non-blocking probes before a wait on the softmax <-> MMA chain sleeps (a few microseconds of polling).
+constexpr int kSpin = 256;
 
 // I8: the Sage core (int8 Q, K with per-block scales). !I8: the fp16 SDPA (fp16 Q, K; fp32 scores; one scale) in the
 // same structure, for the sequences below the Sage threshold.
@@ -60,13 +67,9 @@ struct Sage3Cfg {
 };
 
 // The int32 bits that become -inf once the bias is added: keys past S.
-constexpr uint32_t kMaskedRaw = 0xFF800000u - kBias;
 
-// Non-blocking probes before a wait on the softmax <-> MMA chain sleeps (a few microseconds of polling).
-#ifndef H3_SPIN
-#define H3_SPIN 256
-#endif
-constexpr int kSpin = H3_SPIN;
+
+
 
 // One half row (64 keys) of scores r: keys at or past `valid` are masked. I8: r holds raw int32 sums; masked keys get
 // kMaskedRaw, then the bias is added in place; returns the biased max. !I8: r holds fp32 scores; masked keys get -inf;
@@ -111,13 +114,8 @@ __device__ __forceinline__ float sage3_exp_half(const uint32_t (&r)[2][32], floa
         for (int e = 0; e < 16; ++e) {
             const float2 y = __ffma2_rn(make_float2(__uint_as_float(r[c2][2 * e]), __uint_as_float(r[c2][2 * e + 1])), c2v, k2v);
             float2 p;
-            if ((e & 3) < 4 - kPolyPairs) {
-                p.x = ex2(y.x);
-                p.y = ex2(y.y);
-            } else {
-                p.x = exp2_poly(y.x);
-                p.y = exp2_poly(y.y);
-            }
+            p.x = ex2(y.x);
+            p.y = ex2(y.y);
             sum[e & 3] = __fadd2_rn(sum[e & 3], p);
             pk[c2 * 16 + e] = pack_half2(p.x, p.y);
         }
@@ -270,18 +268,14 @@ __global__ void __launch_bounds__(Sage3Cfg<I8>::THREADS, 1)
         }
         for (int j = 0; j < n_kv && ok; ++j) {
             const bool more = j + 1 < n_kv;
-            if (lane == 0) H3_T(8 + t, j, 0);
             if (!wait_v(j) || (more && !wait_k(j + 1))) { ok = false; break; }
-            if (lane == 0) H3_T(8 + t, j, 1);
             // S_hi of the next key tile as soon as the softmax has read S_hi(j)
             if (more) {
                 if (!warp_wait(hi_free + t, j & 1, a.wait_ns, abort, kSpin)) { ok = false; break; }
                 qk(j + 1, 1);
                 mma_commit_w(hi_full + t);
             }
-            if (lane == 0) H3_T(8 + t, j, 2);
             if (!warp_wait(p_full + t, j & 1, a.wait_ns, abort, kSpin)) { ok = false; break; }
-            if (lane == 0) H3_T(8 + t, j, 3);
             pv(j);
             mma_commit_w(v_empty + j % C::NV);
             if (more) {
@@ -290,7 +284,6 @@ __global__ void __launch_bounds__(Sage3Cfg<I8>::THREADS, 1)
             }
             // the next S_lo, or after the last P.V the phase the epilogue waits for
             mma_commit_w(lo_full + t);
-            if (lane == 0) H3_T(8 + t, j, 4);
         }
         if (!ok && lane == 0) fail(kErrMma);
         mma_commit_w(mma_done + t);
@@ -310,7 +303,6 @@ __global__ void __launch_bounds__(Sage3Cfg<I8>::THREADS, 1)
         const int kpb = a.blk / 64;      // 64-key groups per scale block (1 for the reference's block of 64)
         float m_run = -INFINITY, l_run = 0.0f;
         bool ok = true;
-        const bool tr = lane == 0;
         // the K scales of a tile are loaded one tile ahead
         auto ks_of = [&](int jj, float& lo, float& hi) {
             if (!I8) { lo = hi = 1.0f; return; }
@@ -333,18 +325,15 @@ __global__ void __launch_bounds__(Sage3Cfg<I8>::THREADS, 1)
         auto give_turn = [&] { bar_arrive(t == 0 ? bar_to1 : bar_to0, 64); };
         int turns = 0;                     // turns taken and given back
         for (int j = 0; j < n_kv; ++j) {
-            if (tr) H3_T(warp - 4, j, 6);
             const int kv0 = j * kTileN;
             // c > 0 always (a zero scale gives zero scores either way), so -inf keys stay -inf through the FFMA
             const float c_lo = fmaxf(cq * ks_lo, 1e-30f);
             const float c_hi = fmaxf(cq * ks_hi, 1e-30f);
-            if (tr) H3_T(warp - 4, j, 7);
             // the next tile's scales load into the same registers: nothing waits for them before the next iteration
             ks_of(j + 1, ks_lo, ks_hi);
             const float m_prev = m_run;
 
             // ---- keys 64-127: read, free the columns for the next tile, max, exps (P_hi stays in registers)
-            if (tr) H3_T(warp - 4, j, 0);
             ok = warp_wait(hi_full + t, j & 1, a.wait_ns, abort, kSpin);
             if (!ok) break;
             tc_fence_after();
@@ -355,7 +344,6 @@ __global__ void __launch_bounds__(Sage3Cfg<I8>::THREADS, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(hi_free + t);
-            if (tr) H3_T(warp - 4, j, 1);
             const float bm_hi = sage3_bias_max<I8>(r, S - kv0 - 64);
             const float sm_hi = sage3_scaled_max<I8>(bm_hi, c_hi);
             if (sm_hi > m_run + 8.0f) m_run = sm_hi;             // also the first finite max
@@ -365,7 +353,6 @@ __global__ void __launch_bounds__(Sage3Cfg<I8>::THREADS, 1)
             float sum_hi = sage3_exp_half(r, c_hi, sage3_offset<I8>(c_hi, m_run), p_hi);
             give_turn();
             ++turns;
-            if (tr) H3_T(warp - 4, j, 2);
 
             // ---- keys 0-63: read (after P(j-1).V_{j-1}), max, and where the max moves, scale P_hi down
             ok = warp_wait(lo_full + t, j & 1, a.wait_ns, abort, kSpin);
@@ -374,7 +361,6 @@ __global__ void __launch_bounds__(Sage3Cfg<I8>::THREADS, 1)
             tmem_ld32(t_lane + colS, r[0]);
             tmem_ld32(t_lane + colS + 32, r[1]);
             tmem_wait_ld();
-            if (tr) H3_T(warp - 4, j, 3);
             const float bm_lo = sage3_bias_max<I8>(r, S - kv0);
             const float sm_lo = sage3_scaled_max<I8>(bm_lo, c_lo);
             if (sm_lo > m_run + 8.0f) m_run = sm_lo;
@@ -399,7 +385,6 @@ __global__ void __launch_bounds__(Sage3Cfg<I8>::THREADS, 1)
             tmem_st16(t_lane + colS + 16, *reinterpret_cast<const uint32_t(*)[16]>(&p_lo[16]));
             tmem_st16(t_lane + colS + 32, *reinterpret_cast<const uint32_t(*)[16]>(&p_hi[0]));
             tmem_st16(t_lane + colS + 48, *reinterpret_cast<const uint32_t(*)[16]>(&p_hi[16]));
-            if (tr) H3_T(warp - 4, j, 4);
             // l and O: scaled by 2^(m_prev - m_run) where the max moved in this tile
             const bool grow = m_run != m_prev;
             const float alpha = grow ? (m_prev == -INFINITY ? 0.0f : ex2(m_prev - m_run)) : 1.0f;
@@ -421,7 +406,6 @@ __global__ void __launch_bounds__(Sage3Cfg<I8>::THREADS, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full + t);
-            if (tr) H3_T(warp - 4, j, 5);
         }
         // the turns this warp has left after a failure, without work (the failure is recorded first, so that the
         // other roles stop waiting at once)
@@ -462,26 +446,15 @@ inline cudaError_t launch_sage3(const CUtensorMap& q, const CUtensorMap& k, cons
     return cudaGetLastError();
 }
 
-// The Sage kernel behind every entry point: attn_sage3; H3S_SAGE_KERNEL=2 selects attn_sage2 (one S pass per key tile,
-// max before exps), kept for comparison.
+// The Sage kernel behind every entry point.
 inline cudaError_t launch_sage(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, const AttnArgs& a,
                                cudaStream_t st) {
-    static const int which = [] {
-        const char* e = std::getenv("H3S_SAGE_KERNEL");
-        return e && std::atoi(e) == 2 ? 2 : 3;
-    }();
-    return which == 2 ? launch_sage2(q, k, v, a, st) : launch_sage3<true>(q, k, v, a, 1, st);
+    return launch_sage3<true>(q, k, v, a, 1, st);
 }
-
-// The fp16 SDPA behind every entry point: attn_sage3<false>; H3S_SDPA_KERNEL=1 selects the earlier attn_fwd<false>
-// (one query tile per CTA, max before exps), kept for comparison.
+// The fp16 SDPA behind every entry point.
 inline cudaError_t launch_sdpa(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, const AttnArgs& a, int B,
                                cudaStream_t st) {
-    static const int which = [] {
-        const char* e = std::getenv("H3S_SDPA_KERNEL");
-        return e && std::atoi(e) == 1 ? 1 : 3;
-    }();
-    return which == 1 ? launch_attn<false>(q, k, v, a, B, st) : launch_sage3<false>(q, k, v, a, B, st);
+    return launch_sage3<false>(q, k, v, a, B, st);
 }
 
 }  // namespace h3

@@ -25,7 +25,7 @@
 
 #include "../../include/h3cuda.h"
 #include "../../include/h3sage.h"
-#include "attn.cuh"
+#include "attn_common.cuh"
 #include "prepass.cuh"
 #include "attn3.cuh"
 #include "rmsrope.cuh"

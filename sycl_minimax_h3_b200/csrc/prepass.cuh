@@ -16,7 +16,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
-#include "attn.cuh"
+#include "attn_common.cuh"
 #include "ptx.cuh"
 
 namespace h3 {
