@@ -88,9 +88,11 @@ int h3s_upload_wait(void* ctx);
 /* out = softmax(q . k^T / sqrt(D)) . v, per head. q, k, v: S token rows of H heads x D features, row s at element
  * s * stride (stride >= H * D; 3 * H * D when they sit inside the qkv linear's output), in type dt; out [S, H * D] in
  * out_dt, rounded through half. S >= H3S_SAGE_MIN_S (8192): SageAttention v1 (int8 q, k with per-64-row scales after
- * k's channel mean is taken out; libh3sage.so beside this library); shorter: fp16 SDPA. D = 64 or 128 (other head
- * sizes return -1). S, H or D <= 0:
- * nothing to do, returns 0. No score table is ever written: memory stays O(S * H * D). (kernels/h3sycl.h:190-191) */
+ * k's channel mean is taken out; libh3sage.so beside this library) for D = 64 or 128, as the reference's plugin
+ * (kernels/sage.cpp:33); every other call, and every D from 1 to 128, fp16 SDPA. D > 128 returns -1: a narrowing of
+ * the reference, whose fused path takes any D (kernels/h3sycl.cpp:1464-1573); the engine's heads are 128 (denoiser)
+ * and 64 (VAE). S, H or D <= 0: nothing to do, returns 0. No score table is ever written: memory stays O(S * H * D).
+ * (kernels/h3sycl.h:190-191) */
 int h3s_attention(void* ctx, const void* q, const void* k, const void* v, int dt, int64_t S, int64_t H, int64_t D,
                   int64_t stride, void* out, int out_dt);
 /* B independent sequences of S tokens in one call: sequence b's rows start at row b * S of q, k, v and of out

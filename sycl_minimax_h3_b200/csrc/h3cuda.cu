@@ -235,21 +235,7 @@ int prepass_dt(Ctx& c, const void* q, const void* k, int64_t S, int64_t H, int64
     if ((e = cudaEventRecord(c.ev_fork, c.st)) != cudaSuccess) return cuda_fail("event", e);
     if ((e = cudaStreamWaitEvent(c.aux, c.ev_fork, 0)) != cudaSuccess) return cuda_fail("event", e);
     CUtensorMap map;
-    bool tma = false;
-    if (aligned16(k) && (stride * es) % 16 == 0) {
-        auto enc = tensor_map_encoder();
-        if (enc) {
-            const cuuint64_t dims[2] = {(cuuint64_t) C, (cuuint64_t) S};
-            const cuuint64_t strides[1] = {(cuuint64_t) (stride * es)};
-            const cuuint32_t box[2] = {(cuuint32_t) kMeanCh, (cuuint32_t) kMeanRows};
-            const cuuint32_t estr[2] = {1, 1};
-            const CUtensorMapDataType ty = DT == F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
-                                         : DT == BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-            tma = enc(&map, ty, 2, const_cast<void*>(k), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                      CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
-                  CUDA_SUCCESS;
-        }
-    }
+    const bool tma = aligned16(k) && (stride * es) % 16 == 0 && make_kmean_map<DT>(&map, k, C, S, stride);
     if (tma) {
         using M = MeanCfg<DT>;
         if ((e = cudaFuncSetAttribute(kmean_tma<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, M::SMEM)) != cudaSuccess)
@@ -292,12 +278,13 @@ int prepass(Ctx& c, const void* q, const void* k, int dt, int64_t S, int64_t H, 
 }
 
 // any dt token rows -> half [H, S, D] for one sequence
-int to_half(Ctx& c, const void* src, int dt, int64_t S, int64_t H, int64_t D, int64_t stride, __half* dst) {
+int to_half(Ctx& c, const void* src, int dt, int64_t S, int64_t H, int64_t D, int64_t stride, __half* dst, int64_t Dp = 0) {
     const int blocks = 148 * 8;
+    const int dp = (int) (Dp > 0 ? Dp : D);
     switch (dt) {
-        case F16: to_half_hsd<F16><<<blocks, 256, 0, c.st>>>(src, (int) S, (int) H, (int) D, stride, dst); break;
-        case BF16: to_half_hsd<BF16><<<blocks, 256, 0, c.st>>>(src, (int) S, (int) H, (int) D, stride, dst); break;
-        default: to_half_hsd<F32><<<blocks, 256, 0, c.st>>>(src, (int) S, (int) H, (int) D, stride, dst); break;
+        case F16: to_half_hsd<F16><<<blocks, 256, 0, c.st>>>(src, (int) S, (int) H, (int) D, stride, dst, dp); break;
+        case BF16: to_half_hsd<BF16><<<blocks, 256, 0, c.st>>>(src, (int) S, (int) H, (int) D, stride, dst, dp); break;
+        default: to_half_hsd<F32><<<blocks, 256, 0, c.st>>>(src, (int) S, (int) H, (int) D, stride, dst, dp); break;
     }
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : cuda_fail("to half", e);
@@ -384,31 +371,37 @@ int attention_sage(Ctx& c, const void* q, const void* k, const void* v, int dt, 
 // ---- Form 1: fp16 SDPA over B sequences (kernels/h3sycl.cpp:1464-1674) ------------------------------------------------
 int attention_sdpa(Ctx& c, const void* q, const void* k, const void* v, int dt, int64_t B, int64_t S, int64_t H, int64_t D,
                    int64_t stride, void* out, int out_dt, const OutPeers* peers = nullptr) {
-    if (D != 64 && D != 128) { g_err = "attention: head size " + std::to_string(D) + " (64 or 128 on this build)"; return -1; }
+    // any head size up to the kernel's 128 features: a narrower head is described to TMA with its true width and
+    // reads as zeros beyond it (kernels/h3sycl.cpp:1464-1573 takes any D; wider heads are refused on this build)
+    if (D > kHeadDim) {
+        g_err = "attention: head size " + std::to_string(D) + " (at most " + std::to_string(kHeadDim) + " on this build)";
+        return -1;
+    }
     if (S > INT32_MAX / 2 || B * H > 65535) { g_err = "attention: sequence or head count out of range"; return -1; }
     Phases ph(c);
     ph.mark();
-    const bool inplace = dt == F16 && aligned16(q) && aligned16(k) && aligned16(v) && (stride * 2) % 16 == 0;
+    const bool inplace = dt == F16 && D % 8 == 0 && aligned16(q) && aligned16(k) && aligned16(v) && (stride * 2) % 16 == 0;
     const void *qp = q, *kp = k, *vp = v;
     int order = 1;
     int64_t tok = stride * 2, head = D * 2, seq = S * stride * 2;
     if (!inplace) {
-        const size_t n = (size_t) B * S * H * D;
+        const int64_t Dp = (D + 7) / 8 * 8;          // 16-byte rows
+        const size_t per = (size_t) S * H * Dp, n = (size_t) B * per;
         __half* hq = c.grow(c.hq, c.hq_cap, n);
         __half* hk = c.grow(c.hk, c.hk_cap, n);
         __half* hv = c.grow(c.hv, c.hv_cap, n);
         if (!hq || !hk || !hv) return -1;
-        const size_t ei = (size_t) esize(dt), per = (size_t) S * H * D;
+        const size_t ei = (size_t) esize(dt);
         for (int64_t b = 0; b < B; ++b) {
             const size_t io = (size_t) (b * S * stride) * ei;
-            if (to_half(c, (const char*) q + io, dt, S, H, D, stride, hq + b * per) ||
-                to_half(c, (const char*) k + io, dt, S, H, D, stride, hk + b * per) ||
-                to_half(c, (const char*) v + io, dt, S, H, D, stride, hv + b * per))
+            if (to_half(c, (const char*) q + io, dt, S, H, D, stride, hq + b * per, Dp) ||
+                to_half(c, (const char*) k + io, dt, S, H, D, stride, hk + b * per, Dp) ||
+                to_half(c, (const char*) v + io, dt, S, H, D, stride, hv + b * per, Dp))
                 return -1;
         }
         qp = hq; kp = hk; vp = hv;
         order = 0;
-        tok = D * 2; head = S * D * 2; seq = H * S * D * 2;
+        tok = Dp * 2; head = S * Dp * 2; seq = H * S * Dp * 2;
     }
     ph.mark();
     CUtensorMap mq, mk, mv;
@@ -426,7 +419,8 @@ int attention_sdpa(Ctx& c, const void* q, const void* k, const void* v, int dt, 
     a.out_tok = H * D;
     a.out_head = D;
     a.out_dt = out_dt;
-    a.out_vec = aligned16(out) ? 1 : 0;
+    // 16-byte stores when every 32-feature chunk of every row starts on 16 bytes
+    a.out_vec = aligned16(out) && (D * esize(out_dt)) % 16 == 0 ? 1 : 0;
     if (peers) {   // B = 1
         a.out_rows = (int) (S / peers->P);
         a.out_tok = peers->tok;
@@ -1011,17 +1005,7 @@ int h3s_attention_sage_static(void* stream, const void* q, const void* k, const 
     if ((e = cudaMemsetAsync(err, 0, sizeof(int), st)) != cudaSuccess) return cuda_fail("h3s_attention_sage_static", e);
     // K mean (one chain per channel), then the two quantisers, all on the caller's stream
     CUtensorMap map;
-    auto enc = tensor_map_encoder();
-    bool tma = false;
-    if (enc) {
-        const cuuint64_t dims[2] = {(cuuint64_t) C, (cuuint64_t) S};
-        const cuuint64_t strides[1] = {(cuuint64_t) (stride * 2)};
-        const cuuint32_t box[2] = {(cuuint32_t) kMeanCh, (cuuint32_t) kMeanRows};
-        const cuuint32_t estr[2] = {1, 1};
-        tma = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(k), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-    }
+    const bool tma = make_kmean_map<F16>(&map, k, C, S, stride);
     const uint64_t wait_ns = env_wait_ns();
     if (tma) {
         using M = MeanCfg<F16>;

@@ -2,13 +2,15 @@
 //
 //   kmean     kmean[h*D+d] = (((0 + k_0) + k_1) + ... + k_{S-1}) / (float) S: one fp32 chain per channel in token order
 //             (the reference's loop, kernels/h3sycl.cpp:1733-1737). A chain cannot be split without changing its bits,
-//             so the work is shaped around it: a TMA ring streams 128-token x 32-channel tiles of k into shared memory
-//             (96 KB in flight per CTA) while 32 threads run the 32 chains over each tile.
+//             so the work is shaped around it: a TMA ring streams 256-token x 64-channel tiles of k into shared memory
+//             (96 KB in flight per CTA) while 64 threads run the 64 chains over each tile.
 //   quant     per (head, 64-row block): m = max|x - mean|, inv = m > 0 ? 127/m : 0, scale = m/127,
 //             q = clamp(round(x * inv), -127, 127), round half away from zero (kernels/h3sycl.cpp:1738-1761).
 //             One CTA per block; the 64 x D values are read once with 16-byte loads and held in registers (as the raw
 //             chunks) between the absmax and the quantisation.
-//   to_half   any dt -> half [H, S, D] (kernels/h3sycl.cpp:1762-1764), only where the attention cannot read in place.
+//   to_half   any dt -> half [H, S, D] (kernels/h3sycl.cpp:1762-1764), only where the attention cannot read in place;
+//             rows padded to Dp >= D features (16-byte rows for the TMA maps; the padding is never read: the maps cover
+//             the first D features and TMA fills the rest of a box with zeros).
 //
 // All arithmetic uses the round-to-nearest intrinsics (__fadd_rn, __fsub_rn, __fmul_rn, __fdiv_rn), which the compiler
 // never fuses into FMAs, so the results do not depend on contraction.
@@ -59,34 +61,36 @@ __device__ __forceinline__ void ld16(const void* p, float* out) {
 }
 
 // ---- K mean, TMA ring ----------------------------------------------------------------------------------------------
-constexpr int kMeanCh = 32;          // channels per CTA (one chain per thread): 128 CTAs at H*D = 4096, so that many
-                                     // SMs stream k at once (each chain is latency-bound, one add after the other)
-constexpr int kMeanRows = 128;       // tokens per tile
+constexpr int kMeanCh = 64;          // channels per CTA: 128-byte rows of 16-bit k per token, two chain warps
 constexpr int kMeanRingBytes = 96 * 1024;
-constexpr int kMeanThreads = 32 + kMeanCh;   // warp 0: producer; warp 1: one thread per chain
-static_assert(kMeanCh == 32, "the chains are one warp, which frees a ring stage with one arrival");
+constexpr int kMeanThreads = 32 + kMeanCh;   // warp 0: producer; warps 1-2: one thread per chain
 
 template <int DT>
 struct MeanCfg {
-    static constexpr int TILE = kMeanCh * kMeanRows * DtInfo<DT>::ES;
+    static constexpr int ROWS = DtInfo<DT>::ES == 2 ? 256 : 128;   // tokens per tile: 32 KB
+    static constexpr int TILE = kMeanCh * ROWS * DtInfo<DT>::ES;
     static constexpr int NS = kMeanRingBytes / TILE;
     static constexpr int SMEM = NS * TILE + 2 * NS * 8 + 16 + 128;
 };
 
-// map: 2-D over k, dims (H*D channels, S tokens), row stride in bytes, box (64, 64), no swizzle
+// map: 2-D over k, dims (H*D channels, S tokens), row stride in bytes, box (kMeanCh, MeanCfg<DT>::ROWS), no swizzle.
+// The chain of each thread adds its channel's values of a tile in token order; the next 16 values are read from
+// shared memory while the current 16 are added (the chain's dependent adds set the pace).
 template <int DT>
 __global__ void __launch_bounds__(kMeanThreads) kmean_tma(const __grid_constant__ CUtensorMap map, int S, int C,
                                                           float* kmean, int* err, unsigned long long wait_ns) {
     using M = MeanCfg<DT>;
+    constexpr int ROWS = M::ROWS;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
     uint64_t* full = reinterpret_cast<uint64_t*>(sm + M::NS * M::TILE);
     uint64_t* empty = full + M::NS;
     volatile int* abort = reinterpret_cast<volatile int*>(empty + M::NS);
     const int c0 = blockIdx.x * kMeanCh;
-    const int ntile = (S + kMeanRows - 1) / kMeanRows;
+    const int ntile = (S + ROWS - 1) / ROWS;
     if (threadIdx.x == 0) {
-        for (int i = 0; i < M::NS; ++i) { mbar_init(full + i, 1); mbar_init(empty + i, 1); }   // one arrival: the chain warp
+        // a stage is free once both chain warps have added it
+        for (int i = 0; i < M::NS; ++i) { mbar_init(full + i, 1); mbar_init(empty + i, 2); }
         *abort = 0;
         fence_barrier_init();
     }
@@ -101,7 +105,7 @@ __global__ void __launch_bounds__(kMeanThreads) kmean_tma(const __grid_constant_
                 const int st = t % M::NS;
                 if (t >= M::NS && !mbar_wait(empty + st, ((t / M::NS) - 1) & 1, wait_ns, abort)) { ok = false; break; }
                 mbar_expect_tx(full + st, M::TILE);
-                tma_load_2d(sm + st * M::TILE, &map, full + st, c0, t * kMeanRows);
+                tma_load_2d(sm + st * M::TILE, &map, full + st, c0, t * ROWS);
                 last[st] = t;
             }
             if (!ok) { atomicOr(err, kErrPrepass); *abort = 1; }
@@ -118,21 +122,50 @@ __global__ void __launch_bounds__(kMeanThreads) kmean_tma(const __grid_constant_
             // the whole warp agrees, so that it leaves the loop together (the __syncwarp below needs every lane)
             if (!warp_wait(full + st, (t / M::NS) & 1, wait_ns, abort)) { ok = false; break; }
             const uint8_t* tile = sm + st * M::TILE;
-            const int rows = min(kMeanRows, S - t * kMeanRows);
-            if (rows == kMeanRows) {
-#pragma unroll 16
-                for (int r = 0; r < kMeanRows; ++r)
-                    sum = __fadd_rn(sum, ld1<DT>(tile, (size_t) (r * kMeanCh + c)));
+            const int rows = min(ROWS, S - t * ROWS);
+            if (rows == ROWS) {
+                float a[16], b[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) a[i] = ld1<DT>(tile, (size_t) (i * kMeanCh + c));
+#pragma unroll
+                for (int r = 0; r < ROWS; r += 32) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) b[i] = ld1<DT>(tile, (size_t) ((r + 16 + i) * kMeanCh + c));
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) sum = __fadd_rn(sum, a[i]);
+                    if (r + 32 < ROWS) {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) a[i] = ld1<DT>(tile, (size_t) ((r + 32 + i) * kMeanCh + c));
+                    }
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) sum = __fadd_rn(sum, b[i]);
+                }
             } else {
                 for (int r = 0; r < rows; ++r) sum = __fadd_rn(sum, ld1<DT>(tile, (size_t) (r * kMeanCh + c)));
             }
             __syncwarp();
-            if (c == 0) mbar_arrive(empty + st);
+            if ((c & 31) == 0) mbar_arrive(empty + st);
         }
         if (!ok) { atomicOr(err, kErrPrepass); *abort = 1; }
         else if (c0 + c < C) kmean[c0 + c] = __fdiv_rn(sum, (float) S);
     }
     __syncthreads();
+}
+
+// The TMA map kmean_tma reads k through (k 16-byte aligned, the row stride a multiple of 16 bytes); false when the
+// driver cannot make it (the caller then uses kmean_plain).
+template <int DT>
+inline bool make_kmean_map(CUtensorMap* map, const void* k, int C, int64_t S, int64_t stride) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t) C, (cuuint64_t) S};
+    const cuuint64_t strides[1] = {(cuuint64_t) (stride * DtInfo<DT>::ES)};
+    const cuuint32_t box[2] = {(cuuint32_t) kMeanCh, (cuuint32_t) MeanCfg<DT>::ROWS};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUtensorMapDataType ty = DT == F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                 : DT == BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    return enc(map, ty, 2, const_cast<void*>(k), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // Any alignment: one thread per channel reading k directly (the fallback for strides TMA cannot take).
@@ -223,11 +256,11 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows(const void* src, int
 
 // any dt, token rows -> half [H, S, D] (one sequence)
 template <int DT>
-__global__ void to_half_hsd(const void* src, int S, int H, int D, long long stride, __half* dst) {
+__global__ void to_half_hsd(const void* src, int S, int H, int D, long long stride, __half* dst, int Dp) {
     const size_t n = (size_t) S * H * D;
     for (size_t i = blockIdx.x * (size_t) blockDim.x + threadIdx.x; i < n; i += (size_t) gridDim.x * blockDim.x) {
         const size_t d = i % D, t = (i / D) % S, hh = i / ((size_t) D * S);
-        dst[i] = __float2half_rn(ld1<DT>(src, t * (size_t) stride + hh * D + d));
+        dst[(hh * S + t) * Dp + d] = __float2half_rn(ld1<DT>(src, t * (size_t) stride + hh * D + d));
     }
 }
 

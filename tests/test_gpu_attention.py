@@ -183,9 +183,9 @@ def test_error_behaviour(cuda):
     assert L.h3s_attention(ctx.handle, 0, 0, 0, native.F16, 0, 2, 128, 256, 0, native.F16) == 0
     assert L.h3s_attention(ctx.handle, 0, 0, 0, native.F16, 10, 2, 128, 255, 0, native.F16) == -1
     assert "stride" in native.last_error()
-    x = torch.zeros(10, 256, dtype=torch.float16, device=cuda)
-    # head sizes other than 64 and 128 (the reference plugin's bounds, kernels/sage.cpp:33)
-    assert L.h3s_attention(ctx.handle, x.data_ptr(), x.data_ptr(), x.data_ptr(), native.F16, 10, 1, 96, 256,
+    x = torch.zeros(10, 512, dtype=torch.float16, device=cuda)
+    # heads wider than the kernel's 128 features (a stated narrowing: the reference's fused path takes any D)
+    assert L.h3s_attention(ctx.handle, x.data_ptr(), x.data_ptr(), x.data_ptr(), native.F16, 10, 1, 160, 512,
                            x.data_ptr(), native.F16) == -1
     assert "head size" in native.last_error()
     assert L.h3s_attention(ctx.handle, x.data_ptr(), x.data_ptr(), x.data_ptr(), 7, 10, 1, 128, 256, x.data_ptr(),
@@ -245,3 +245,16 @@ def test_context_memory_and_copies(cuda):
         assert info["mem_bytes"] > 0 and ":" in info["pci"]
     finally:
         ctx.close()
+
+
+@pytest.mark.parametrize("D", [8, 12, 32, 48, 80, 96, 100, 120])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_other_head_sizes(D, dtype, cuda):
+    """Head sizes other than 64 and 128 (kernels/h3sycl.cpp:1464-1573 takes any D; the Sage plugin only 64 and 128,
+    kernels/sage.cpp:33, so these run on the fp16 SDPA at every length): heads whose rows are not 16-byte multiples go
+    through the padded half copy, the others are read in place; the output's last chunk of features is partial."""
+    for S, min_s in ((300, None), (200, 0)):          # the default threshold, and a forced Sage request that falls back
+        H = 3
+        qkv = make_qkv(S, H, D, seed=S + D, dtype=dtype)
+        out = run_attention(qkv.to(cuda), H, D, min_s=min_s)
+        check_attention(qkv, out, H, D, sage=False)
