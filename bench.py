@@ -199,7 +199,7 @@ def main() -> None:
     ap.add_argument("--quick", action="store_true", help="main workload only (no c1/c2/c4 side numbers)")
     ap.add_argument("--S", type=int, default=47232, help="tokens of the main workload (profiling runs use a smaller case)")
     ap.add_argument("--H", type=int, default=32, help="heads of the main workload")
-    ap.add_argument("--only", choices=["c1", "c2", "rms_rope", "causal", "int8_linear", "vae"],
+    ap.add_argument("--only", choices=["c1", "c2", "rms_rope", "rope_prepass", "causal", "int8_linear", "vae"],
                     help="run one side leg alone and print its numbers (for profiling that kernel); no bench line")
     args = ap.parse_args()
     if args.impl == "reference":
@@ -246,11 +246,12 @@ def main() -> None:
             res = int8_linear_leg(dev, S, peaks, max_over_ranks, barrier)
         elif args.only == "vae":
             res = vae_leg(dev, max_over_ranks, barrier)
-        elif args.only == "rms_rope":
+        elif args.only in ("rms_rope", "rope_prepass"):
             g = torch.Generator(device=dev)
             g.manual_seed(1000)
             qkv = torch.randn(S, 3 * h * D, generator=g, device=dev, dtype=torch.float16)
-            res = rms_rope_leg(dev, qkv, S, h, D, peaks, max_over_ranks, barrier)
+            leg = rms_rope_leg if args.only == "rms_rope" else rope_prepass_leg
+            res = leg(dev, qkv, S, h, D, peaks, max_over_ranks, barrier)
         else:
             res = side_leg(args.only, dev, h, H, D, max_over_ranks, barrier)
         if rank == 0:
@@ -445,6 +446,7 @@ def main() -> None:
         for name in ("c2", "c1"):
             extra[name] = side_leg(name, dev, h, H, D, max_over_ranks, barrier)
         extra["rms_rope"] = rms_rope_leg(dev, pool[0], S, h, D, peaks, max_over_ranks, barrier)
+        extra["rope_prepass"] = rope_prepass_leg(dev, pool[0], S, h, D, peaks, max_over_ranks, barrier)
         extra["causal"] = causal_leg(dev, max_over_ranks, barrier)
         extra["int8_linear"] = int8_linear_leg(dev, S, peaks, max_over_ranks, barrier)
         extra["vae"] = vae_leg(dev, max_over_ranks, barrier)
@@ -551,6 +553,57 @@ def rms_rope_leg(dev, qkv, S, h, D, peaks, max_over_ranks, barrier, rot=96) -> d
     return {"kernel": "rms_rope_staged<f16> (q and k, two launches)", "S": S, "heads": h, "rot_dim": rot,
             "ms_q_and_k": ms, "algorithmic_GBs": nbytes / (ms / 1e3) / 1e9, "peak_hbm_GBs": peaks["hbm_gbs"],
             "frac": nbytes / (ms / 1e3) / 1e9 / peaks["hbm_gbs"]}
+
+
+def rope_prepass_leg(dev, qkv, S, h, D, peaks, max_over_ranks, barrier, rot=96) -> dict:
+    """The block's step before the attention and the Sage pre-pass (dit.rs:347-350): h3s_rms_rope on q and on k then
+    h3s_sage_prepass, against the fused h3s_sage_prepass_rope (q normalised inside its quantiser's pass). The rows are
+    rotated again on every call (values stay finite: the RMS norm rescales them), the same work each time."""
+    import torch
+
+    from sycl_minimax_h3_b200 import native, ops
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(4243)
+    wq = (1 + 0.1 * torch.randn(D, generator=g, device=dev)).float()
+    wk = (1 + 0.1 * torch.randn(D, generator=g, device=dev)).float()
+    ang = torch.rand(S, rot // 2, generator=g, device=dev) * 6.28
+    cs = torch.stack([torch.cos(ang), torch.sin(ang)], -1).float().contiguous()
+    nb = (S + 63) // 64
+    iq = torch.empty(h, S, D, dtype=torch.int8, device=dev)
+    ik = torch.empty_like(iq)
+    sc = torch.empty(2 * h * nb + h * D, dtype=torch.float32, device=dev)
+    ctx = ops.context(dev)
+    st, qp, kp = 3 * h * D, qkv.data_ptr(), qkv.data_ptr() + h * D * 2
+
+    def separate():
+        ctx.rms_rope(qp, native.F16, S, h, D, st, wq.data_ptr(), 1e-5, cs.data_ptr(), rot)
+        ctx.rms_rope(kp, native.F16, S, h, D, st, wk.data_ptr(), 1e-5, cs.data_ptr(), rot)
+        ctx.sage_prepass(qp, kp, native.F16, S, h, D, st, iq.data_ptr(), ik.data_ptr(), sc.data_ptr())
+
+    def fused():
+        ctx.sage_prepass_rope(qp, kp, native.F16, S, h, D, st, wq.data_ptr(), wk.data_ptr(), 1e-5, cs.data_ptr(), rot,
+                              iq.data_ptr(), ik.data_ptr(), sc.data_ptr())
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = 10
+        e0.record(torch.cuda.current_stream())
+        for _ in range(n):
+            fn()
+        e1.record(torch.cuda.current_stream())
+        torch.cuda.synchronize()
+        ctx.wait()
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1)) / n
+
+    ms_sep, ms_fused = timed(separate), timed(fused)
+    return {"kernels": "rms_rope_staged (q, k) + kmean_tma (priority stream) || quant_rows (q), then quant_rows (k)", "S": S, "heads": h,
+            "rot_dim": rot, "ms_rms_rope_then_prepass": ms_sep, "ms_fused": ms_fused}
 
 
 def causal_leg(dev, max_over_ranks, barrier, L=512, Hq=32, Hkv=8, D=128) -> dict:

@@ -17,9 +17,6 @@
  *   H3S_POISON                 fill new buffers with 0xff bytes (NaN) to expose reads of unwritten memory
  *   H3S_WAIT_MS                limit of every wait inside a kernel (default 2000); past it the kernel stops and
  *                              h3s_wait reports the failure
- *   H3S_SAGE_KERNEL=2          run the earlier Sage kernel (attn_sage2) instead of attn_sage3, for comparison
- *                              (read once per process; libh3sage.so reads it too)
- *   H3S_SDPA_KERNEL=1          run the earlier fp16 kernel (attn_fwd) instead of attn_sage3's fp16 form, for comparison
  */
 #ifndef H3CUDA_H
 #define H3CUDA_H
@@ -174,6 +171,19 @@ int h3s_attention_ulysses(void* ctx, const void* q, const void* k, const void* v
  * mean [H*D], nb = ceil(S / 64). D = 64 or 128. Queued on the context's stream. */
 int h3s_sage_prepass(void* ctx, const void* q, const void* k, int dt, int64_t S, int64_t H, int64_t D, int64_t stride,
                      int8_t* iq, int8_t* ik, float* sc);
+/* h3s_rms_rope(q, wq), h3s_rms_rope(k, wk), then h3s_sage_prepass, in one call with the same results bit for bit (q
+ * and k are left normalised and rotated in place, as the two calls leave them). eps, cs and rot_dim as h3s_rms_rope,
+ * with its refusals. */
+int h3s_sage_prepass_rope(void* ctx, void* q, void* k, int dt, int64_t S, int64_t H, int64_t D, int64_t stride,
+                          const float* wq, const float* wk, float eps, const float* cs, int rot_dim, int8_t* iq,
+                          int8_t* ik, float* sc);
+/* A denoiser block's three calls before its output projection (engine/h3-core/src/dit.rs:347-350), in one:
+ * h3s_rms_rope(q, wq), h3s_rms_rope(k, wk), h3s_attention(q, k, v, ..., out). The Sage path runs the fused pre-pass
+ * above; the fp16 SDPA path normalises q and k first. q and k are left normalised and rotated in place either way;
+ * the output is h3s_attention's on those rows. The refusals of both calls. */
+int h3s_attention_rms_rope(void* ctx, void* q, void* k, const void* v, int dt, int64_t S, int64_t H, int64_t D,
+                           int64_t stride, void* out, int out_dt, const float* wq, const float* wk, float eps,
+                           const float* cs, int rot_dim);
 /* The CUDA stream a context queues on (a cudaStream_t), for callers that order their own work with it. */
 void* h3s_stream(void* ctx);
 /* Self-test of the kernels' bounded waits: queues a kernel that waits `wait_ns` nanoseconds for an mbarrier nothing

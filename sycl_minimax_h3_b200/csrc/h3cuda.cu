@@ -135,7 +135,11 @@ bool init(Ctx& c) {
     if (const char* e = std::getenv("H3S_SAGE_MIN_S")) c.sage_min_s = std::max<int64_t>(0, std::atoll(e));
     c.wait_ns = env_wait_ns();
     cudaError_t e;
-    if ((e = cudaStreamCreateWithFlags(&c.aux, cudaStreamNonBlocking)) != cudaSuccess ||
+    // the K mean (a few dozen CTAs, each a chain of S dependent adds: the pre-pass's critical path) runs on a stream of
+    // the highest priority, so that its CTAs get SMs before the quantisers' thousands of CTAs queued beside it
+    int prio_low = 0, prio_high = 0;
+    cudaDeviceGetStreamPriorityRange(&prio_low, &prio_high);
+    if ((e = cudaStreamCreateWithPriority(&c.aux, cudaStreamNonBlocking, prio_high)) != cudaSuccess ||
         (e = cudaEventCreateWithFlags(&c.ev_fork, cudaEventDisableTiming)) != cudaSuccess ||
         (e = cudaEventCreateWithFlags(&c.ev_join, cudaEventDisableTiming)) != cudaSuccess ||
         (e = cudaMalloc(&c.err, sizeof(int))) != cudaSuccess || (e = cudaMemset(c.err, 0, sizeof(int))) != cudaSuccess) {
@@ -220,10 +224,24 @@ struct Phases {
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 int esize(int dt) { return dt == F32 ? 4 : 2; }
 
+// The step before the attention in a denoiser block (engine/h3-core/src/dit.rs:347-348): RMS norm + RoPE of q and k in
+// place (h3s_rms_rope, kernels/h3sycl.cpp:1276-1376), with q's and k's norm weights.
+struct RopeArgs {
+    const float* wq;
+    const float* wk;
+    float eps;
+    const float* cs;
+    int rot;
+};
+
 // ---- the Sage pre-pass (kernels/h3sycl.cpp:1733-1761) --------------------------------------------------------------
+// With rope: q and k are first normalised and rotated in place by the rms_rope kernel, as two h3s_rms_rope calls would
+// (the same bits), before the K mean forks off. (A single pass that normalises q inside its quantiser, saving one read
+// of q, measured slower at configs[3]: its rotation is compute-bound and, running beside the K mean, slows the K mean's
+// chains, the pre-pass's critical path; the quantiser that runs there now is memory-bound.)
 template <int DT>
 int prepass_dt(Ctx& c, const void* q, const void* k, int64_t S, int64_t H, int64_t D, int64_t stride, int8_t* iq, int8_t* ik,
-               float* sc) {
+               float* sc, const RopeArgs* rope = nullptr) {
     const int64_t nb = (S + kSageBlock - 1) / kSageBlock;
     float* qs = sc;
     float* ks = sc + H * nb;
@@ -231,6 +249,14 @@ int prepass_dt(Ctx& c, const void* q, const void* k, int64_t S, int64_t H, int64
     const int C = (int) (H * D);
     const int es = DtInfo<DT>::ES;
     cudaError_t e;
+    if (rope) {
+        if ((e = launch_rms_rope<DT>(const_cast<void*>(q), S, (int) H, (int) D, stride, rope->wq, rope->eps, rope->cs,
+                                     rope->rot, c.st)) != cudaSuccess)
+            return cuda_fail("rms_rope q", e);
+        if ((e = launch_rms_rope<DT>(const_cast<void*>(k), S, (int) H, (int) D, stride, rope->wk, rope->eps, rope->cs,
+                                     rope->rot, c.st)) != cudaSuccess)
+            return cuda_fail("rms_rope k", e);
+    }
     // fork: the K mean runs on the aux stream beside the Q quantiser
     if ((e = cudaEventRecord(c.ev_fork, c.st)) != cudaSuccess) return cuda_fail("event", e);
     if ((e = cudaStreamWaitEvent(c.aux, c.ev_fork, 0)) != cudaSuccess) return cuda_fail("event", e);
@@ -267,12 +293,12 @@ int prepass_dt(Ctx& c, const void* q, const void* k, int64_t S, int64_t H, int64
 }
 
 int prepass(Ctx& c, const void* q, const void* k, int dt, int64_t S, int64_t H, int64_t D, int64_t stride, int8_t* iq,
-            int8_t* ik, float* sc) {
+            int8_t* ik, float* sc, const RopeArgs* rope = nullptr) {
     if (D != 64 && D != 128) { g_err = "the Sage pre-pass takes D = 64 or 128 (got " + std::to_string(D) + ")"; return -1; }
     switch (dt) {
-        case F16: return prepass_dt<F16>(c, q, k, S, H, D, stride, iq, ik, sc);
-        case BF16: return prepass_dt<BF16>(c, q, k, S, H, D, stride, iq, ik, sc);
-        case F32: return prepass_dt<F32>(c, q, k, S, H, D, stride, iq, ik, sc);
+        case F16: return prepass_dt<F16>(c, q, k, S, H, D, stride, iq, ik, sc, rope);
+        case BF16: return prepass_dt<BF16>(c, q, k, S, H, D, stride, iq, ik, sc, rope);
+        case F32: return prepass_dt<F32>(c, q, k, S, H, D, stride, iq, ik, sc, rope);
         default: g_err = "unknown element type " + std::to_string(dt); return -1;
     }
 }
@@ -312,7 +338,8 @@ struct OutPeers {
 };
 
 int attention_sage(Ctx& c, const void* q, const void* k, const void* v, int dt, int64_t S, int64_t H, int64_t D,
-                   int64_t stride, void* out, int out_dt, const OutPeers* peers = nullptr) {
+                   int64_t stride, void* out, int out_dt, const OutPeers* peers = nullptr, const RopeArgs* rope = nullptr,
+                   bool* rotated = nullptr) {
     if ((D != 64 && D != 128) || S > INT32_MAX / D / H) return 1;   // the plugin's bounds (kernels/sage.cpp:33-35)
     if (peers && !c.sage_peers) return 1;
     const size_t n = (size_t) S * H * D;
@@ -323,7 +350,8 @@ int attention_sage(Ctx& c, const void* q, const void* k, const void* v, int dt, 
     if (!iq || !ik || !sc) return -1;
     Phases ph(c);
     ph.mark();
-    if (prepass(c, q, k, dt, S, H, D, stride, iq, ik, sc) != 0) return -1;
+    if (prepass(c, q, k, dt, S, H, D, stride, iq, ik, sc, rope) != 0) return -1;
+    if (rope && rotated) *rotated = true;
     // v in place when the kernel can read it (half, 16-byte aligned rows); else a half copy by head
     const void* vp = v;
     int64_t v_tok = stride, v_head = D;
@@ -482,6 +510,15 @@ uint8_t* static_scratch(int dev) {
         g_static_ptr[dev] = static_cast<uint8_t*>(p);
     }
     return g_static_ptr[dev];
+}
+
+// h3s_rms_rope's refusals (kernels/h3sycl.cpp:1279-1283)
+bool check_rope(const char* who, int64_t D, int rot_dim) {
+    if (rot_dim < 0 || rot_dim > D || rot_dim % 2 != 0 || (D - rot_dim) % 2 != 0) {
+        g_err = std::string(who) + ": rot_dim must be even, at most D, and leave an even remainder";
+        return false;
+    }
+    return true;
 }
 
 }  // namespace
@@ -958,6 +995,51 @@ int h3s_sage_prepass(void* ctx, const void* q, const void* k, int dt, int64_t S,
     if (!check_dt(dt)) { g_err = "h3s_sage_prepass: unknown element type"; return -1; }
     DeviceGuard g(c.device);
     return prepass(c, q, k, dt, S, H, D, stride, iq, ik, sc);
+}
+
+// h3s_rms_rope on q and on k, then h3s_sage_prepass, with q's normalisation fused into its quantiser's pass
+// (include/h3cuda.h)
+int h3s_sage_prepass_rope(void* ctx, void* q, void* k, int dt, int64_t S, int64_t H, int64_t D, int64_t stride,
+                          const float* wq, const float* wk, float eps, const float* cs, int rot_dim, int8_t* iq,
+                          int8_t* ik, float* sc) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    if (S <= 0 || H <= 0 || D <= 0) return 0;
+    if (!check_rope("h3s_sage_prepass_rope", D, rot_dim)) return -1;
+    if (stride < H * D) { g_err = "h3s_sage_prepass_rope: the row stride is shorter than a row"; return -1; }
+    if (!check_dt(dt)) { g_err = "h3s_sage_prepass_rope: unknown element type"; return -1; }
+    DeviceGuard g(c.device);
+    const RopeArgs rope{wq, wk, eps, cs, rot_dim};
+    return prepass(c, q, k, dt, S, H, D, stride, iq, ik, sc, &rope);
+}
+
+// The attention half of a denoiser block's step before its output projection (engine/h3-core/src/dit.rs:347-350):
+// h3s_rms_rope(q), h3s_rms_rope(k), h3s_attention, in one call (include/h3cuda.h)
+int h3s_attention_rms_rope(void* ctx, void* q, void* k, const void* v, int dt, int64_t S, int64_t H, int64_t D,
+                           int64_t stride, void* out, int out_dt, const float* wq, const float* wk, float eps,
+                           const float* cs, int rot_dim) {
+    auto& c = *static_cast<Ctx*>(ctx);
+    if (S <= 0 || H <= 0 || D <= 0) return 0;
+    if (!check_rope("h3s_attention_rms_rope", D, rot_dim)) return -1;
+    if (stride < H * D) { g_err = "h3s_attention_rms_rope: the row stride is shorter than a row"; return -1; }
+    if (!check_dt(dt) || !check_dt(out_dt)) { g_err = "h3s_attention_rms_rope: unknown element type"; return -1; }
+    DeviceGuard g(c.device);
+    const RopeArgs rope{wq, wk, eps, cs, rot_dim};
+    bool rotated = false;
+    if (c.sage_want && S >= c.sage_min_s && sage_load(c)) {
+        const int rc = attention_sage(c, q, k, v, dt, S, H, D, stride, out, out_dt, nullptr, &rope, &rotated);
+        if (rc == 0) return 0;
+        if (rc == -1) return -1;
+        if (rc == -2) {   // as h3s_attention: log, wait, stay on the SDPA kernel from now on
+            std::fprintf(stderr, "h3cuda: SageAttention failed (%s); attention stays on the fp16 SDPA kernel\n", g_err.c_str());
+            cudaStreamSynchronize(c.st);
+            c.sage_state = -1;
+        }
+    }
+    if (!rotated) {   // the SDPA path reads q and k as they are: normalise and rotate them first (once)
+        if (h3s_rms_rope(ctx, q, dt, S, H, D, stride, wq, eps, cs, rot_dim) != 0) return -1;
+        if (h3s_rms_rope(ctx, k, dt, S, H, D, stride, wk, eps, cs, rot_dim) != 0) return -1;
+    }
+    return attention_sdpa(c, q, k, v, dt, 1, S, H, D, stride, out, out_dt);
 }
 
 void* h3s_stream(void* ctx) { return (void*) static_cast<Ctx*>(ctx)->st; }

@@ -52,6 +52,8 @@ CUDA_SYMBOLS = [
     ("h3s_ulysses_push_out", I, [P, P, I64, I64, I64, I, I, I, P]),
     ("h3s_attention_ulysses", I, [P, P, P, P, I, I64, I64, I64, I64, P, I, I, I]),
     ("h3s_sage_prepass", I, [P, P, P, I, I64, I64, I64, I64, P, P, P]),
+    ("h3s_sage_prepass_rope", I, [P, P, P, I, I64, I64, I64, I64, P, P, ctypes.c_float, P, I, P, P, P]),
+    ("h3s_attention_rms_rope", I, [P, P, P, P, I, I64, I64, I64, I64, P, I, P, P, ctypes.c_float, P, I]),
     ("h3s_stream", P, [P]),
     ("h3s_selftest_wait_timeout", I, [P, U64]),
     ("h3s_attention_sage_static", I, [P, P, P, P, I64, I64, I64, I64, P, I, P]),
@@ -250,6 +252,16 @@ class Context:
 
     def sage_prepass(self, q: int, k: int, dt: int, S: int, H: int, D: int, stride: int, iq: int, ik: int, sc: int) -> None:
         check(self._lib.h3s_sage_prepass(self.handle, q, k, dt, S, H, D, stride, iq, ik, sc), "h3s_sage_prepass")
+
+    def sage_prepass_rope(self, q: int, k: int, dt: int, S: int, H: int, D: int, stride: int, wq: int, wk: int,
+                          eps: float, cs: int, rot_dim: int, iq: int, ik: int, sc: int) -> None:
+        check(self._lib.h3s_sage_prepass_rope(self.handle, q, k, dt, S, H, D, stride, wq, wk, eps, cs, rot_dim, iq, ik,
+                                              sc), "h3s_sage_prepass_rope")
+
+    def attention_rms_rope(self, q: int, k: int, v: int, dt: int, S: int, H: int, D: int, stride: int, out: int,
+                           out_dt: int, wq: int, wk: int, eps: float, cs: int, rot_dim: int) -> None:
+        check(self._lib.h3s_attention_rms_rope(self.handle, q, k, v, dt, S, H, D, stride, out, out_dt, wq, wk, eps, cs,
+                                               rot_dim), "h3s_attention_rms_rope")
 
     def selftest_wait_timeout(self, wait_ns: int) -> None:
         check(self._lib.h3s_selftest_wait_timeout(self.handle, wait_ns), "h3s_selftest_wait_timeout")

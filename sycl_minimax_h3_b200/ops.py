@@ -159,3 +159,18 @@ def attention_batch(q: Rows, k: Rows, v: Rows, seqs: int, out: torch.Tensor) -> 
     ctx = context(out.device)
     ctx.attention_batch(q.ptr(), k.ptr(), v.ptr(), dt_code(q.t.dtype), seqs, q.tokens // seqs, q.heads, q.dim, q.stride,
                         out.data_ptr(), dt_code(out.dtype))
+
+
+def attention_rms_rope(q: Rows, k: Rows, v: Rows, out: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tensor,
+                       eps: float, cs: torch.Tensor, rot_dim: int) -> None:
+    """A denoiser block's ``rms_rope(q)``, ``rms_rope(k)``, ``attention(q, k, v, out)`` in one call (dit.rs:347-350):
+    q and k are left normalised and rotated in place, as the two ``rms_rope`` calls leave them."""
+    if q.layout() != k.layout() or q.layout() != v.layout():
+        raise H3Error("attention_rms_rope: q, k and v must have the same layout")
+    if out.numel() != q.tokens * q.heads * q.dim or not out.is_contiguous():
+        raise H3Error(f"attention_rms_rope: out {list(out.shape)} for {q.tokens} tokens of {q.heads} x {q.dim}")
+    ctx = context(out.device)
+    ctx.attention_rms_rope(q.ptr(), k.ptr(), v.ptr(), dt_code(q.t.dtype), q.tokens, q.heads, q.dim, q.stride,
+                           out.data_ptr(), dt_code(out.dtype), _floats(q_norm, "the q norm weight", q.dim),
+                           _floats(k_norm, "the k norm weight", q.dim), eps,
+                           _floats(cs, "the rotation table", q.tokens * rot_dim), rot_dim)
