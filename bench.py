@@ -297,6 +297,7 @@ def main() -> None:
     ctx.wait()
     if not bool(torch.isfinite(out).all()):
         raise SystemExit("bench: the timed attention produced non-finite values; no number is reported")
+    parity = parity_rows(pool[(args.warmup + args.steps - 1) % len(pool)], out, S, h, D, seed=rank)
     barrier()
     ms_total = max_over_ranks(e0.elapsed_time(e1))
     ms_call = ms_total / args.steps
@@ -466,6 +467,7 @@ def main() -> None:
             "config": bench_config(S, H, D, world, min(nblocks, args.warmup + args.steps)),
             "ms_per_call": ms_call, "pct_int8_peak_measured_x2": value / world / (2 * peaks["bf16_tflops"]),
             "roofline": roofline, "prepass": prepass, "e2e": e2e, "gpu_launches": launches_per_call * args.steps,
+            "parity": parity,
             "clocks": clk.summary(), "extra": extra,
         }
         if cpu is not None:
@@ -477,6 +479,35 @@ def main() -> None:
 
 
 SIDE = {"c2": (16848, True), "c1": (2159, False)}     # tokens, Sage path (else the fp16 SDPA)
+
+
+def parity_rows(qkv, out, S: int, H: int, D: int, n: int = 512, seed: int = 0) -> dict:
+    """The output's error on n sampled (head, token) rows, every head covered, against float64 softmax attention of the
+    same fp16 inputs computed with torch on the GPU: min per-row cosine and max-abs error (the tolerance the north star
+    states: cosine >= 0.999, max-abs stated). Not timed."""
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    rh = torch.arange(n) % H
+    rs = torch.randint(0, S, (n,), generator=g)
+    rs[0], rs[-1] = 0, S - 1
+    x = qkv.view(S, 3, H, D)
+    cos_min, abs_max = 1.0, 0.0
+    for h in range(H):
+        sel = rs[rh == h].to(qkv.device)
+        if sel.numel() == 0:
+            continue
+        q = x[sel, 0, h].double()
+        k = x[:, 1, h].double()
+        v = x[:, 2, h].double()
+        p = torch.softmax((q @ k.T) / D ** 0.5, dim=-1)
+        want = p @ v
+        got = out.view(S, H, D)[sel, h].double()
+        cos = torch.nn.functional.cosine_similarity(got, want, dim=-1)
+        cos_min = min(cos_min, float(cos.min()))
+        abs_max = max(abs_max, float((got - want).abs().max()))
+    return {"rows": n, "min_cos_vs_float64": cos_min, "max_abs_vs_float64": abs_max,
+            "reference": "float64 softmax attention of the same inputs (torch, on the GPU), sampled rows of every head"}
 
 
 def side_leg(name, dev, h, H, D, max_over_ranks, barrier) -> dict:
@@ -512,8 +543,9 @@ def side_leg(name, dev, h, H, D, max_over_ranks, barrier) -> dict:
         if not sage_path:
             os.environ.pop("H3S_SAGE_MIN_S", None)
             ops._ctx.clear()
+    parity = parity_rows(qkv2, out2, S2, h, D, seed=S2)
     return {"S": S2, "H": H, "ms_per_call": ms2, "tops": ops_per_call(S2, H, D) / (ms2 / 1e3) / 1e12,
-            "path": "sage" if sage_path else "fp16 sdpa"}
+            "path": "sage" if sage_path else "fp16 sdpa", "parity": parity}
 
 
 def rms_rope_leg(dev, qkv, S, h, D, peaks, max_over_ranks, barrier, rot=96) -> dict:

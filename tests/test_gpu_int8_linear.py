@@ -209,3 +209,30 @@ def test_refusals_and_degenerate_sizes(cuda):
         ops.Int8Linear(w, ws).forward(x, torch.zeros(4, 9, device=cuda).half())
     with pytest.raises(native.H3Error, match="must be int8"):
         ops.Int8Linear(w.float(), ws).forward(x, out)
+
+
+def test_one_sm_gemm_variant_bit_exact(tmp_path):
+    """The one-SM GEMM (i8gemm, H3S_LIN_KERNEL=1: read once per process, so a child process) gives the same bits as
+    the oracle, as the SM-pair kernel the product runs by default does."""
+    import os
+    import subprocess
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = f"""
+import sys
+sys.path[:0] = [{root!r}, {os.path.join(root, 'oracle')!r}, {os.path.join(root, 'tests')!r}]
+import numpy as np, torch
+import oracle
+from test_gpu_int8_linear import inputs, run, bits, CODE
+cuda = torch.device("cuda", 0)
+for (M, K, N, dt, group) in ((300, 512, 700, torch.bfloat16, 256), (129, 1024, 260, torch.float16, 32), (70, 136, 300, torch.bfloat16, 0)):
+    x, w, ws, b = inputs(M, K, N, dt, seed=M + K, per_n=True)
+    got = run(x, w, ws, b, dt, group, cuda)
+    want = oracle.int8_linear(bits(x), CODE[dt], M, K, w.numpy(), N, ws.numpy(), b.numpy(), CODE[dt], group)
+    assert np.array_equal(bits(got), want), (M, K, N)
+print("ok")
+"""
+    env = dict(os.environ, H3S_LIN_KERNEL="1")
+    res = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=600)
+    assert res.returncode == 0 and res.stdout.strip().endswith("ok"), res.stdout[-2000:] + res.stderr[-2000:]
