@@ -4,8 +4,9 @@ tokens, % of the int8 tensor peak, 1/2/4/8 GPUs).
 One step = one h3s_attention call of the 47,232-token case (c3: 32 heads x 128, fp16 q/k/v as the strided parts of a
 qkv buffer, fp16 out), with a fresh seeded input per denoiser block (50 blocks, each > L2). With N GPUs (torchrun), the
 32 heads are split over the ranks (32/N heads each, no exchange: heads are independent), so the total work is fixed
-(strong scaling). Also reported: c2 (16,848 tokens, Sage), c1 (2,159 tokens, fp16 SDPA) and, for N > 1, the Ulysses
-variant c4 (token-sharded activations, NCCL all-to-all to head shards and back) with its exposed all-to-all time.
+(strong scaling). Also reported: c2 (16,848 tokens, Sage), c1 (2,159 tokens, fp16 SDPA), each leg's parity against
+float64 on sampled rows, the neighbouring kernels, and for N > 1 the Ulysses variant c4 (token-sharded activations,
+exchanged to head shards and back over peer memory, NCCL's all-to-all timed beside it) with its exposed exchange time.
 
 --impl reference times the reference's attention restated on the CPU (oracle/, the reference itself cannot be built
 here) on the host cores, rank 0 only, on a bounded sample of the same workload.
