@@ -173,7 +173,7 @@ int h3s_sage_prepass(void* ctx, const void* q, const void* k, int dt, int64_t S,
                      int8_t* iq, int8_t* ik, float* sc);
 /* h3s_rms_rope(q, wq), h3s_rms_rope(k, wk), then h3s_sage_prepass, in one call with the same results bit for bit (q
  * and k are left normalised and rotated in place, as the two calls leave them). eps, cs and rot_dim as h3s_rms_rope,
- * with its refusals. */
+ * with its refusals; D = 64 or 128, as h3s_sage_prepass. */
 int h3s_sage_prepass_rope(void* ctx, void* q, void* k, int dt, int64_t S, int64_t H, int64_t D, int64_t stride,
                           const float* wq, const float* wk, float eps, const float* cs, int rot_dim, int8_t* iq,
                           int8_t* ik, float* sc);
