@@ -377,14 +377,21 @@ __global__ void __launch_bounds__(Sage3Cfg<I8>::THREADS, 1)
                 }
             }
             uint32_t p_lo[32];
+            // P_hi goes to TMEM columns 32-63 (S_lo's, read above). The fp16 kernel issues those stores inside its lo
+            // turn, before the exps: measured 15-20 % shorter (32 heads x 8,192 tokens: 0.86-0.92 ms against
+            // 1.08-1.12 ms). The int8 kernel is no faster that way and keeps them after the lo stores.
+            auto store_p_hi = [&] {
+                tmem_st16(t_lane + colS + 32, *reinterpret_cast<const uint32_t(*)[16]>(&p_hi[0]));
+                tmem_st16(t_lane + colS + 48, *reinterpret_cast<const uint32_t(*)[16]>(&p_hi[16]));
+            };
             take_turn(false);
+            if constexpr (!I8) store_p_hi();
             const float sum_lo = sage3_exp_half(r, c_lo, sage3_offset<I8>(c_lo, m_run), p_lo);
             give_turn();
             ++turns;
             tmem_st16(t_lane + colS, *reinterpret_cast<const uint32_t(*)[16]>(&p_lo[0]));
             tmem_st16(t_lane + colS + 16, *reinterpret_cast<const uint32_t(*)[16]>(&p_lo[16]));
-            tmem_st16(t_lane + colS + 32, *reinterpret_cast<const uint32_t(*)[16]>(&p_hi[0]));
-            tmem_st16(t_lane + colS + 48, *reinterpret_cast<const uint32_t(*)[16]>(&p_hi[16]));
+            if constexpr (I8) store_p_hi();
             // l and O: scaled by 2^(m_prev - m_run) where the max moved in this tile
             const bool grow = m_run != m_prev;
             const float alpha = grow ? (m_prev == -INFINITY ? 0.0f : ex2(m_prev - m_run)) : 1.0f;
