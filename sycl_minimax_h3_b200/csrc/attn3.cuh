@@ -64,12 +64,8 @@ struct Sage3Cfg {
                                             : idesc(kFmtF32, kFmtF16, kFmtF16, 0, 0, kTileM, 64);
     static constexpr uint32_t IDESC_PV = idesc(kFmtF32, kFmtF16, kFmtF16, 0, 1, kTileM, kHeadDim);
     static_assert(SMEM <= 232448, "shared memory budget of one sm_100 CTA");
+    static_assert(8 * kStageWarpBytes <= OFF_V, "the output stage of the 8 softmax warps fits in Q and the K ring");
 };
-
-// The int32 bits that become -inf once the bias is added: keys past S.
-
-
-
 
 // One half row (64 keys) of scores r: keys at or past `valid` are masked. I8: r holds raw int32 sums; masked keys get
 // kMaskedRaw, then the bias is added in place; returns the biased max. !I8: r holds fp32 scores; masked keys get -inf;
@@ -429,7 +425,11 @@ __global__ void __launch_bounds__(Sage3Cfg<I8>::THREADS, 1)
             if (lane == 0) fail(kErrSoftmax);
         } else {
             tc_fence_after();
-            store_out_row(a, b, h, qrow, t_lane + colO, 1.0f / l_run, qrow < S);
+            // every Q.K^T MMA of both tiles is complete here (the other tile's last S_lo was read before this
+            // warp's last turn or the hand-back above), so Q and the K ring are free to stage the output rows
+            if (a.out_vec) store_out_staged(a, b, h, qrow - lane, lane, t_lane + colO, 1.0f / l_run,
+                                            sm + C::OFF_Q + (warp - 4) * kStageWarpBytes);
+            else store_out_row(a, b, h, qrow, t_lane + colO, 1.0f / l_run, qrow < S);
         }
     }
 

@@ -136,6 +136,94 @@ __device__ __forceinline__ void store_out_row(const AttnArgs& a, int b, int h, i
     store_out_cols(a, b, h, qrow, o_taddr, inv, live, 0, 4);
 }
 
+// The output rows of one warp through shared memory. A thread owns one query row, so direct 16-byte stores put 32
+// rows' chunks in each warp store (32 cache lines per instruction); staged, each store instruction writes 512
+// consecutive bytes of two rows.
+constexpr int kStagePitch = 272;                  // 256 bytes of a row + 16: the 32 rows' 16-byte chunks in distinct banks
+constexpr int kStageWarpBytes = 32 * kStagePitch;
+
+// 32 O columns scaled by inv, rounded through half (kernels/h3sycl.cpp:1769-1771) and packed in the out type:
+// 16 words for F16 / BF16, 32 for F32. Packed conversions (two values per instruction, each rounded to nearest even).
+__device__ __forceinline__ void pack_out32(int out_dt, const uint32_t (&o)[32], float inv, uint32_t (&w)[32]) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+        const __half2 h2 = __floats2half2_rn(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv);
+        if (out_dt == F16) {
+            w[i / 2] = *reinterpret_cast<const uint32_t*>(&h2);
+        } else {
+            const float2 f = __half22float2(h2);
+            if (out_dt == BF16) {
+                const __nv_bfloat162 b2 = __floats2bfloat162_rn(f.x, f.y);
+                w[i / 2] = *reinterpret_cast<const uint32_t*>(&b2);
+            } else {
+                w[i] = __float_as_uint(f.x);
+                w[i + 1] = __float_as_uint(f.y);
+            }
+        }
+    }
+}
+
+// Rows row0 .. row0+31 (this lane: row0 + lane) of O at o_taddr, times inv, to the output. stage: this warp's
+// kStageWarpBytes of shared memory that nothing else uses any more. Needs a.out_vec (16-byte aligned rows whose byte
+// length is a multiple of 16). Rows at or past S are not stored.
+__device__ __forceinline__ void store_out_staged(const AttnArgs& a, int b, int h, int row0, int lane, uint32_t o_taddr,
+                                                 float inv, uint8_t* stage) {
+    const int esz = a.out_dt == F32 ? 4 : 2;
+    const int cpp = 256 / esz;                         // columns per pass: 256 bytes of each row
+    // this lane's row: its first byte in the output (null past S)
+    uint8_t* dst = nullptr;
+    {
+        const int q = row0 + lane;
+        if (q < a.S) {
+            void* out = a.out;
+            int row = q;
+            if (a.out_rows > 0) {
+                const int p = q / a.out_rows;
+                row = q - p * a.out_rows;
+                out = a.out_peer[p & 7];
+            }
+            dst = reinterpret_cast<uint8_t*>(out) +
+                  ((long long) b * a.out_seq + (long long) row * a.out_tok + (long long) h * a.out_head) * esz;
+        }
+    }
+    fence_proxy_async_smem();                          // the stage held TMA-written, MMA-read tiles
+    for (int col0 = 0; col0 < a.D; col0 += cpp) {
+        const int ncols = min(cpp, a.D - col0);
+        const int upr = ncols * esz / 16;              // 16-byte chunks of each row in this pass (at most 16)
+#pragma unroll
+        for (int c = 0; c < 4; c += 2) {
+            if (c * 32 >= ncols) break;                // the same for the whole warp (tcgen05.ld is warp-wide)
+            uint32_t o[2][32];
+            tmem_ld32(o_taddr + col0 + c * 32, o[0]);
+            if ((c + 1) * 32 < ncols) tmem_ld32(o_taddr + col0 + (c + 1) * 32, o[1]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                if ((c + k) * 32 >= ncols) break;
+                uint32_t w[32];
+                pack_out32(a.out_dt, o[k], inv, w);
+                const int nb = min(32, ncols - (c + k) * 32) * esz;
+                uint4* sd = reinterpret_cast<uint4*>(stage + lane * kStagePitch + (c + k) * 32 * esz);
+#pragma unroll
+                for (int v = 0; v < 8; ++v)
+                    if (v * 16 < nb) sd[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+            }
+        }
+        __syncwarp();
+        // two rows per store instruction: lanes 0-15 row r, lanes 16-31 row r + 1, lane & 15 the 16-byte chunk
+        const int chunk = lane & 15;
+#pragma unroll
+        for (int r = 0; r < 32; r += 2) {
+            const int rr = r + (lane >> 4);
+            uint8_t* d = reinterpret_cast<uint8_t*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(dst), rr));
+            if (d != nullptr && chunk < upr)
+                *reinterpret_cast<uint4*>(d + col0 * esz + chunk * 16) =
+                    *reinterpret_cast<const uint4*>(stage + rr * kStagePitch + chunk * 16);
+        }
+        __syncwarp();
+    }
+}
+
 // max of 32 values with three-input max instructions (a tree: 16 instructions, depth 4)
 __device__ __forceinline__ float max32(const uint32_t (&r)[32]) {
     float m[11];

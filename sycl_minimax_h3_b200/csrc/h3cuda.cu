@@ -260,17 +260,7 @@ int prepass_dt(Ctx& c, const void* q, const void* k, int64_t S, int64_t H, int64
     // fork: the K mean runs on the aux stream beside the Q quantiser
     if ((e = cudaEventRecord(c.ev_fork, c.st)) != cudaSuccess) return cuda_fail("event", e);
     if ((e = cudaStreamWaitEvent(c.aux, c.ev_fork, 0)) != cudaSuccess) return cuda_fail("event", e);
-    CUtensorMap map;
-    const bool tma = aligned16(k) && (stride * es) % 16 == 0 && make_kmean_map<DT>(&map, k, C, S, stride);
-    if (tma) {
-        using M = MeanCfg<DT>;
-        if ((e = cudaFuncSetAttribute(kmean_tma<DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, M::SMEM)) != cudaSuccess)
-            return cuda_fail("kmean", e);
-        kmean_tma<DT><<<(C + kMeanCh - 1) / kMeanCh, kMeanThreads, M::SMEM, c.aux>>>(map, (int) S, C, kmean, c.err, c.wait_ns);
-    } else {
-        kmean_plain<DT><<<(C + 127) / 128, 128, 0, c.aux>>>(k, (int) S, C, (long long) stride, kmean);
-    }
-    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail("kmean launch", e);
+    if ((e = launch_kmean<DT>(k, S, C, stride, kmean, c.err, c.wait_ns, c.aux)) != cudaSuccess) return cuda_fail("kmean", e);
     if ((e = cudaEventRecord(c.ev_join, c.aux)) != cudaSuccess) return cuda_fail("event", e);
     const dim3 grid((unsigned) nb, (unsigned) H);
     const bool vq = aligned16(q) && (stride * es) % 16 == 0 && (D * es) % 16 == 0;
@@ -452,6 +442,7 @@ int attention_sdpa(Ctx& c, const void* q, const void* k, const void* v, int dt, 
     if (peers) {   // B = 1
         a.out_rows = (int) (S / peers->P);
         a.out_tok = peers->tok;
+        if ((peers->tok * esize(out_dt)) % 16 != 0) a.out_vec = 0;
         for (int p = 0; p < peers->P; ++p) {
             a.out_peer[p] = peers->p[p];
             if (!aligned16(peers->p[p])) a.out_vec = 0;
@@ -1086,17 +1077,9 @@ int h3s_attention_sage_static(void* stream, const void* q, const void* k, const 
     // the caller's error word starts each call at zero (a set word makes the attention kernel skip its work)
     if ((e = cudaMemsetAsync(err, 0, sizeof(int), st)) != cudaSuccess) return cuda_fail("h3s_attention_sage_static", e);
     // K mean (one chain per channel), then the two quantisers, all on the caller's stream
-    CUtensorMap map;
-    const bool tma = make_kmean_map<F16>(&map, k, C, S, stride);
     const uint64_t wait_ns = env_wait_ns();
-    if (tma) {
-        using M = MeanCfg<F16>;
-        if ((e = cudaFuncSetAttribute(kmean_tma<F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, M::SMEM)) != cudaSuccess)
-            return cuda_fail("h3s_attention_sage_static", e);
-        kmean_tma<F16><<<(C + kMeanCh - 1) / kMeanCh, kMeanThreads, M::SMEM, st>>>(map, (int) S, C, kmean, err, wait_ns);
-    } else {
-        kmean_plain<F16><<<(C + 127) / 128, 128, 0, st>>>(k, (int) S, C, (long long) stride, kmean);
-    }
+    if ((e = launch_kmean<F16>(k, S, C, stride, kmean, err, wait_ns, st)) != cudaSuccess)
+        return cuda_fail("h3s_attention_sage_static", e);
     const dim3 grid((unsigned) nb, (unsigned) H);
     quant_rows<F16, 128, true><<<grid, kQuantThreads, 0, st>>>(q, (int) S, stride, nullptr, iq, qs, (int) nb);
     quant_rows<F16, 128, true><<<grid, kQuantThreads, 0, st>>>(k, (int) S, stride, kmean, ik, ks, (int) nb);
