@@ -740,7 +740,7 @@ def vae_leg(dev, max_over_ranks, barrier, B=4, S=1797, H=32, D=64) -> dict:
     barrier()
     ms = max_over_ranks(e0.elapsed_time(e1)) / n
     flops = 4.0 * S * S * D * H * B
-    return {"kernel": "attn_sage3<false> (fp16 SDPA, batch in the grid)", "B": B, "S": S, "H": H, "D": D, "ms": ms,
+    return {"kernel": "attn_sage3<false, 64> (fp16 SDPA, 64-wide heads, batch in the grid)", "B": B, "S": S, "H": H, "D": D, "ms": ms,
             "tflops": flops / (ms / 1e3) / 1e12}
 
 

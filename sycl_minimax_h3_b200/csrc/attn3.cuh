@@ -6,9 +6,9 @@
 // issuer of tile 1 (each whole warp runs its loop, elect.sync picks the issuing lane); 2 TMA producer of the ring of
 // half V tiles; 4-7 softmax of query tile 0, 8-11 of tile 1 (one thread per query row; warp w reads TMEM lane quarter
 // w % 4). The same kernel, instantiated with I8 = false, is the fp16 SDPA (fp16 Q.K^T, fp32 scores, one scale).
-// TMEM (512 columns): S0 0-127, S1 128-255, O0 256-383, O1 384-511. In S_t, columns 0-63 hold the scores of keys 0-63
-// of a key tile (S_lo) and then P_t of all 128 keys (half, two per column); columns 64-127 hold the scores of keys
-// 64-127 (S_hi).
+// TMEM (512 columns): S0 0-127, S1 128-255, O0 256-383, O1 384-511 (64-wide heads: O0 256-319, O1 320-383). In S_t,
+// columns 0-63 hold the scores of keys 0-63 of a key tile (S_lo) and then P_t of all 128 keys (half, two per column);
+// columns 64-127 hold the scores of keys 64-127 (S_hi).
 //
 // The chain of one query tile t and key tile j (int8 Q.K^T on tcgen05 kind::i8 into int32, P.V on kind::f16):
 //   1. the softmax loads S_hi(j) and at once lets the MMA thread issue S_hi(j+1) = Q_t.K_{j+1}[64:128)^T into the same
@@ -41,15 +41,20 @@ constexpr uint32_t kMaskedRaw = 0xFF800000u - kBias;
 constexpr int kSpin = 256;
 
 // I8: the Sage core (int8 Q, K with per-block scales). !I8: the fp16 SDPA (fp16 Q, K; fp32 scores; one scale) in the
-// same structure, for the sequences below the Sage threshold.
-template <bool I8>
+// same structure, for the sequences below the Sage threshold. HD: the head width the kernel computes, 128, or 64 for
+// the fp16 SDPA of heads up to 64 wide (the VAE's): Q.K^T with K = 64, P.V with N = 64, 16 KB tiles and deeper rings,
+// O in 64 TMEM columns per tile.
+template <bool I8, int HD = kHeadDim>
 struct Sage3Cfg {
+    static_assert(HD == kHeadDim || (!I8 && HD == 64), "64-wide heads on the fp16 path only");
     static constexpr int NQ = 2;                             // query tiles per CTA
     static constexpr int CB_BYTES = 128 * 128;               // one column block: 128 rows x 128 bytes, 128-byte swizzle
-    static constexpr int TILE_B = I8 ? CB_BYTES : 2 * CB_BYTES;   // a 128-row Q or K tile (int8: 1 block, fp16: 2)
-    static constexpr int V_BYTES = kTileN * kHeadDim * 2;    // 32 KB, two column blocks of 64 features
-    static constexpr int NK = I8 ? 4 : 3, NV = I8 ? 3 : 2;   // (fp16: the 32 KB K tiles leave room for fewer stages)
-    static constexpr int KSTEPS = I8 ? 4 : 8;                // MMAs per 64-key half of Q.K^T (K = 32 int8 / 16 fp16)
+    static constexpr int NCB = I8 ? 1 : HD / 64;             // column blocks of a Q or K tile (int8: 128 features)
+    static constexpr int TILE_B = NCB * CB_BYTES;            // a 128-row Q or K tile
+    static constexpr int V_BYTES = kTileN * HD * 2;          // column blocks of 64 features
+    static constexpr int NK = I8 ? 4 : (HD == 64 ? 6 : 3);   // (fp16: the 32 KB K tiles of 128-wide heads leave room
+    static constexpr int NV = I8 ? 3 : (HD == 64 ? 4 : 2);   //  for fewer stages)
+    static constexpr int KSTEPS = I8 ? 4 : HD / 16;          // MMAs per 64-key half of Q.K^T (K = 32 int8 / 16 fp16)
     static constexpr int OFF_Q = 0;
     static constexpr int OFF_K = OFF_Q + NQ * TILE_B;
     static constexpr int OFF_V = OFF_K + NK * TILE_B;
@@ -62,7 +67,7 @@ struct Sage3Cfg {
     static constexpr int THREADS = 384;
     static constexpr uint32_t IDESC_QK = I8 ? idesc(kFmtS32, kFmtS8, kFmtS8, 0, 0, kTileM, 64)   // one half: N = 64 keys
                                             : idesc(kFmtF32, kFmtF16, kFmtF16, 0, 0, kTileM, 64);
-    static constexpr uint32_t IDESC_PV = idesc(kFmtF32, kFmtF16, kFmtF16, 0, 1, kTileM, kHeadDim);
+    static constexpr uint32_t IDESC_PV = idesc(kFmtF32, kFmtF16, kFmtF16, 0, 1, kTileM, HD);
     static_assert(SMEM <= 232448, "shared memory budget of one sm_100 CTA");
     static_assert(8 * kStageWarpBytes <= OFF_V, "the output stage of the 8 softmax warps fits in Q and the K ring");
 };
@@ -120,11 +125,11 @@ __device__ __forceinline__ float sage3_exp_half(const uint32_t (&r)[2][32], floa
     return s.x + s.y;
 }
 
-template <bool I8>
-__global__ void __launch_bounds__(Sage3Cfg<I8>::THREADS, 1)
+template <bool I8, int HD = kHeadDim>
+__global__ void __launch_bounds__(Sage3Cfg<I8, HD>::THREADS, 1)
     attn_sage3(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
-    using C = Sage3Cfg<I8>;
+    using C = Sage3Cfg<I8, HD>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bar = reinterpret_cast<uint64_t*>(sm + C::OFF_BAR);
@@ -208,7 +213,7 @@ __global__ void __launch_bounds__(Sage3Cfg<I8>::THREADS, 1)
                                  j * kTileN, h, b);
                 } else {
                     mbar_expect_tx(full + st, C::V_BYTES);
-                    for (int cb = 0; cb < 2; ++cb)
+                    for (int cb = 0; cb < HD / 64; ++cb)
                         tma_rows(sm + C::OFF_V + st * C::V_BYTES + cb * C::CB_BYTES, &tmV, full + st, a.v_order, cb * 64,
                                  j * kTileN, h, b);
                 }
@@ -248,7 +253,7 @@ __global__ void __launch_bounds__(Sage3Cfg<I8>::THREADS, 1)
             const uint32_t v_base = smem_u32(sm + C::OFF_V + sv * C::V_BYTES);
 #pragma unroll
             for (int kk = 0; kk < kTileN / 16; ++kk)
-                mma_ts_f16_w(tmem + 2 * kTileN + t * kHeadDim, tmem + t * kTileN + kk * 8,
+                mma_ts_f16_w(tmem + 2 * kTileN + t * HD, tmem + t * kTileN + kk * 8,
                              sdesc(v_base + (uint32_t) (kk * 16 * 128), C::CB_BYTES, 1024), C::IDESC_PV,
                              (j > 0 || kk > 0) ? 1u : 0u);
         };
@@ -291,7 +296,7 @@ __global__ void __launch_bounds__(Sage3Cfg<I8>::THREADS, 1)
         const int wq = warp & 3;                      // the TMEM lane quarter this warp may touch
         const int row = wq * 32 + lane;
         const uint32_t t_lane = tmem + ((uint32_t) (wq * 32) << 16);
-        const uint32_t colS = (uint32_t) (t * kTileN), colO = (uint32_t) (2 * kTileN + t * kHeadDim);
+        const uint32_t colS = (uint32_t) (t * kTileN), colO = (uint32_t) (2 * kTileN + t * HD);
         const int qrow = q0 + t * kTileM + row;
         const int S = a.S;
         const float cq = I8 ? a.qs[(size_t) h * a.nb + min(qrow, S - 1) / a.blk] * a.scale_log2 : a.scale_log2;
@@ -396,7 +401,7 @@ __global__ void __launch_bounds__(Sage3Cfg<I8>::THREADS, 1)
             if (__any_sync(0xffffffffu, grow && j > 0)) {
                 const float al = j > 0 ? alpha : 1.0f;
 #pragma unroll
-                for (int c4 = 0; c4 < 4; ++c4) {
+                for (int c4 = 0; c4 < HD / 32; ++c4) {
                     uint32_t o[32];
                     tmem_ld32(t_lane + colO + c4 * 32, o);
                     tmem_wait_ld();
@@ -442,14 +447,14 @@ __global__ void __launch_bounds__(Sage3Cfg<I8>::THREADS, 1)
 }
 
 // grid (query-tile pairs, heads x sequences)
-template <bool I8>
+template <bool I8, int HD = kHeadDim>
 inline cudaError_t launch_sage3(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, const AttnArgs& a,
                                 int B, cudaStream_t st) {
-    using C = Sage3Cfg<I8>;
-    cudaError_t e = cudaFuncSetAttribute(attn_sage3<I8>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    using C = Sage3Cfg<I8, HD>;
+    cudaError_t e = cudaFuncSetAttribute(attn_sage3<I8, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return e;
     dim3 grid((unsigned) ((a.S + C::NQ * kTileM - 1) / (C::NQ * kTileM)), (unsigned) (a.H * B));
-    attn_sage3<I8><<<grid, C::THREADS, C::SMEM, st>>>(q, k, v, a);
+    attn_sage3<I8, HD><<<grid, C::THREADS, C::SMEM, st>>>(q, k, v, a);
     return cudaGetLastError();
 }
 
@@ -458,10 +463,10 @@ inline cudaError_t launch_sage(const CUtensorMap& q, const CUtensorMap& k, const
                                cudaStream_t st) {
     return launch_sage3<true>(q, k, v, a, 1, st);
 }
-// The fp16 SDPA behind every entry point.
+// The fp16 SDPA behind every entry point: the 64-wide form for heads up to 64 wide.
 inline cudaError_t launch_sdpa(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, const AttnArgs& a, int B,
                                cudaStream_t st) {
-    return launch_sage3<false>(q, k, v, a, B, st);
+    return a.D <= 64 ? launch_sage3<false, 64>(q, k, v, a, B, st) : launch_sage3<false>(q, k, v, a, B, st);
 }
 
 }  // namespace h3
