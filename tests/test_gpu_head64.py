@@ -1,10 +1,10 @@
 """Head size 64 on the GPU through the C ABI against the oracle: the reference plugin takes D in {64, 128}
 (kernels/sage.cpp:33) and the fp16 path serves the VAE's 64-wide heads (kernels/h3sycl.cpp:1581-1674).
 
-The kernels run 128 wide and read a 64-wide head as zeros in features 64-127 (TMA fills outside the tensor with zeros),
-so these tests also pin that the padding changes nothing: the same tolerances as for D = 128 (per-row cosine >= 0.999
-and max-abs <= 0.05 against float64 softmax; >= 0.9999 against the oracle's restatement of the same arithmetic), and
-the pre-pass bit-exact."""
+The Sage kernel runs 128 wide and reads a 64-wide head as zeros in features 64-127 (TMA fills outside the tensor with
+zeros); the fp16 SDPA runs a 64-wide instantiation (K = 64 Q.K^T, N = 64 P.V, 64 TMEM columns of O per tile). Both
+are held to the same tolerances as D = 128 (per-row cosine >= 0.999 and max-abs <= 0.05 against float64 softmax;
+>= 0.9999 against the oracle's restatement of the same arithmetic), and the pre-pass is bit-exact."""
 import ctypes
 
 import numpy as np
@@ -35,6 +35,20 @@ def test_sdpa_path_d64(S, cuda):
     qkv = make_qkv(S, H, D, seed=650 + S)
     out = run_attention(qkv.to(cuda), H, D, min_s=1 << 30)
     check_attention(qkv, out, H, D, sage=False)
+
+
+@pytest.mark.parametrize("dtype,out_dtype", [(torch.bfloat16, torch.bfloat16), (torch.float32, torch.float32),
+                                             (torch.float16, torch.float32), (torch.float16, torch.bfloat16)])
+@pytest.mark.parametrize("min_s", [0, 1 << 30])
+def test_element_types_d64(dtype, out_dtype, min_s, cuda):
+    """Every input and output type on both paths; the output rounded through half first (kernels/h3sycl.cpp:1769-1771)."""
+    S, H = 333, 2
+    qkv = make_qkv(S, H, D, seed=67, dtype=dtype)
+    out = run_attention(qkv.to(cuda), H, D, out_dtype=out_dtype, min_s=min_s)
+    assert out.dtype == out_dtype
+    check_attention(qkv, out, H, D, sage=min_s == 0)
+    o = out.float()
+    assert torch.equal(o, o.half().float())
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
