@@ -38,9 +38,10 @@ struct AttnArgs {
     int q_order, k_order, v_order;   // 0: map dims (D, S, H, B); 1: map dims (D, H, S, B)
     int* err;                   // device error word
     unsigned long long wait_ns; // limit of every wait
-    int D;                      // head size, 64 or 128: the kernels run 128 wide, and a 64-wide head reads as zeros in
-                                // features 64-127 (TMA fills what lies outside the tensor with zeros), so those
-                                // features of Q.K^T add nothing and those of P.V come out 0 and are not stored
+    int D;                      // head size: the kernel runs 128 wide (64 wide for the fp16 path's heads up to 64),
+                                // and a narrower head reads as zeros in the features past D (TMA fills what lies
+                                // outside the tensor with zeros), so those features of Q.K^T add nothing and those of
+                                // P.V come out 0 and are not stored
     // Output rows spread over the ranks of a Ulysses group (out_rows > 0): token s goes to out_peer[s / out_rows], a
     // rank's token shard in its own or another GPU's memory (base already at this rank's head columns), at row
     // s % out_rows; out is then unused. out_rows = 0: every row to out.
