@@ -218,6 +218,20 @@ inline cudaError_t launch_kmean(const void* k, int64_t S, int C, int64_t stride,
 }
 
 // ---- quantiser -----------------------------------------------------------------------------------------------------
+// The packed pair type of a 16-bit element type, its NaN and its exact widening.
+template <int DT> struct Half2Of;
+template <> struct Half2Of<F16> {
+    using T = __half2;
+    static __device__ __forceinline__ T nan2() { return __halves2half2(__ushort_as_half(0x7E00), __ushort_as_half(0x7E00)); }
+    static __device__ __forceinline__ float2 to_float2(T v) { return __half22float2(v); }
+};
+template <> struct Half2Of<BF16> {
+    using T = __nv_bfloat162;
+    static __device__ __forceinline__ T nan2() {
+        return __halves2bfloat162(__ushort_as_bfloat16(0x7FC0), __ushort_as_bfloat16(0x7FC0));
+    }
+    static __device__ __forceinline__ float2 to_float2(T v) { return __bfloat1622float2(v); }
+};
 constexpr int kQuantThreads = 128;
 
 // grid (nb, H); src rows at element stride `stride`, head h at column h*D; dst int8 [H, S, D]; scales [H, nb].
@@ -256,13 +270,43 @@ __global__ void __launch_bounds__(kQuantThreads) quant_rows(const void* src, int
         }
     }
     float m = 0.0f;
+    if constexpr (DtInfo<DT>::ES == 2) {
+        // x -> __fsub_rn(x, mean) is monotone, so over this thread's rows the largest |x - mean| of a channel is at the
+        // channel's largest or smallest value: those two, found on the 16-bit values (exact, two channels per
+        // instruction), are all that is converted and subtracted. The min/max start at NaN and skip NaN, as fmaxf
+        // below skips a NaN |x - mean|, so the result has the bits of the per-element loop.
+        using T2 = typename Half2Of<DT>::T;
+        T2 hi[EPC / 2], lo[EPC / 2];
 #pragma unroll
-    for (int i = 0; i < NCH; ++i) {
-        if (rsub + i * RSTEP < rows) {
-            float x[EPC];
-            ld16<DT>(&raw[i], x);
+        for (int p = 0; p < EPC / 2; ++p) hi[p] = lo[p] = Half2Of<DT>::nan2();
 #pragma unroll
-            for (int e = 0; e < EPC; ++e) m = fmaxf(m, fabsf(__fsub_rn(x[e], mu[e])));
+        for (int i = 0; i < NCH; ++i) {
+            if (rsub + i * RSTEP < rows) {
+                const T2* v = reinterpret_cast<const T2*>(&raw[i]);
+#pragma unroll
+                for (int p = 0; p < EPC / 2; ++p) {
+                    hi[p] = __hmax2(hi[p], v[p]);
+                    lo[p] = __hmin2(lo[p], v[p]);
+                }
+            }
+        }
+#pragma unroll
+        for (int p = 0; p < EPC / 2; ++p) {
+            const float2 a = Half2Of<DT>::to_float2(hi[p]), c = Half2Of<DT>::to_float2(lo[p]);
+            m = fmaxf(m, fabsf(__fsub_rn(a.x, mu[2 * p])));
+            m = fmaxf(m, fabsf(__fsub_rn(c.x, mu[2 * p])));
+            m = fmaxf(m, fabsf(__fsub_rn(a.y, mu[2 * p + 1])));
+            m = fmaxf(m, fabsf(__fsub_rn(c.y, mu[2 * p + 1])));
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < NCH; ++i) {
+            if (rsub + i * RSTEP < rows) {
+                float x[EPC];
+                ld16<DT>(&raw[i], x);
+#pragma unroll
+                for (int e = 0; e < EPC; ++e) m = fmaxf(m, fabsf(__fsub_rn(x[e], mu[e])));
+            }
         }
     }
     // block absmax

@@ -124,3 +124,26 @@ def gpu_prepass(qkv: torch.Tensor, H: int, D: int, stride: int | None = None, dt
 
 __all__ = ["make_qkv", "bits", "run_attention", "check_attention", "attention_stats", "gpu_prepass", "sample_rows", "tok_rows_to_head_rows",
            "half_bits_to_f32", "MIN_ROW_COSINE", "MAX_ABS_VS_EXACT"]
+
+
+def edge_qkv(S: int, H: int, D: int, dtype: torch.dtype, seed: int = 0) -> torch.Tensor:
+    """q | k | v rows with the values a quantiser's absmax can mishandle: NaN (scattered, and a whole channel of one
+    64-row block), +-inf, -0, subnormals, the largest finite values, and blocks of zeros; S need not be a multiple of 64."""
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(S, 3 * H * D, generator=g) * 2
+    big = 65504.0 if dtype == torch.float16 else 3.0e38
+    tiny = 6.0e-8 if dtype == torch.float16 else 1.0e-39
+    n = S * 3 * H * D
+    idx = torch.randperm(n, generator=g)
+    flat = x.view(-1)
+    flat[idx[: n // 200]] = float("nan")
+    flat[idx[n // 200: n // 100]] = float("inf")
+    flat[idx[n // 100: n // 70]] = -float("inf")
+    flat[idx[n // 70: n // 50]] = -0.0
+    flat[idx[n // 50: n // 40]] = big * torch.sign(torch.randn(n // 40 - n // 50, generator=g))
+    flat[idx[n // 40: n // 30]] = tiny
+    x[:64, 5] = float("nan")                       # one q channel all NaN in the first block
+    x[64:128, H * D + 7] = float("nan")            # one k channel all NaN in the second block
+    if S > 128:
+        x[128:min(S, 192), :H * D] = 0.0           # a block of zeros (scale 0, codes 0)
+    return x.to(dtype)

@@ -77,6 +77,21 @@ def test_prepass_edge_values():
     assert all(same(a, b) for a, b in zip(mine, ref))
 
 
+@pytest.mark.parametrize("dt", [oracle.F16, oracle.BF16])
+@pytest.mark.parametrize("D", [64, 128])
+def test_prepass_nan_inf_values(dt, D):
+    """NaN, +-inf, -0, subnormals and an all-NaN channel in a block (the inputs of the GPU edge test): the oracle's
+    pre-pass has the reference's bits."""
+    import torch
+    from _util import edge_qkv
+    S, H = 200, 2
+    t = edge_qkv(S, H, D, torch.float16 if dt == oracle.F16 else torch.bfloat16, seed=D)
+    x = bits(t)
+    mine, ref = both(x, dt, S, H, D, 3 * H * D)
+    for name, a, b in zip(("iq", "ik", "qs", "ks", "kmean", "hv"), mine, ref):
+        assert same(a, b), f"{name} differs from the reference's own pre-pass"
+
+
 def test_prepass_c0():
     """8 heads x 2,048 tokens, fp16."""
     S, H, D = 2048, 8, 128
