@@ -37,9 +37,6 @@ namespace h3 {
 // The int32 bits that become -inf once the bias is added: keys past S.
 constexpr uint32_t kMaskedRaw = 0xFF800000u - kBias;
 
-// Non-blocking probes before a wait on the softmax <-> MMA chain sleeps (a few microseconds of polling).
-constexpr int kSpin = 256;
-
 // I8: the Sage core (int8 Q, K with per-block scales). !I8: the fp16 SDPA (fp16 Q, K; fp32 scores; one scale) in the
 // same structure, for the sequences below the Sage threshold. HD: the head width the kernel computes, 128, or 64 for
 // the fp16 SDPA of heads up to 64 wide (the VAE's): Q.K^T with K = 64, P.V with N = 64, 16 KB tiles and deeper rings,
@@ -257,8 +254,8 @@ __global__ void __launch_bounds__(Sage3Cfg<I8, HD>::THREADS, 1)
                              sdesc(v_base + (uint32_t) (kk * 16 * 128), C::CB_BYTES, 1024), C::IDESC_PV,
                              (j > 0 || kk > 0) ? 1u : 0u);
         };
-        auto wait_k = [&](int j) { return warp_wait(k_full + j % C::NK, (j / C::NK) & 1, a.wait_ns, abort, kSpin); };
-        auto wait_v = [&](int j) { return warp_wait(v_full + j % C::NV, (j / C::NV) & 1, a.wait_ns, abort, kSpin); };
+        auto wait_k = [&](int j) { return warp_wait(k_full + j % C::NK, (j / C::NK) & 1, a.wait_ns, abort); };
+        auto wait_v = [&](int j) { return warp_wait(v_full + j % C::NV, (j / C::NV) & 1, a.wait_ns, abort); };
         ok = ok && wait_k(0);
         if (ok) {
             qk(0, 1);
@@ -272,11 +269,11 @@ __global__ void __launch_bounds__(Sage3Cfg<I8, HD>::THREADS, 1)
             if (!wait_v(j) || (more && !wait_k(j + 1))) { ok = false; break; }
             // S_hi of the next key tile as soon as the softmax has read S_hi(j)
             if (more) {
-                if (!warp_wait(hi_free + t, j & 1, a.wait_ns, abort, kSpin)) { ok = false; break; }
+                if (!warp_wait(hi_free + t, j & 1, a.wait_ns, abort)) { ok = false; break; }
                 qk(j + 1, 1);
                 mma_commit_w(hi_full + t);
             }
-            if (!warp_wait(p_full + t, j & 1, a.wait_ns, abort, kSpin)) { ok = false; break; }
+            if (!warp_wait(p_full + t, j & 1, a.wait_ns, abort)) { ok = false; break; }
             pv(j);
             mma_commit_w(v_empty + j % C::NV);
             if (more) {
@@ -335,7 +332,7 @@ __global__ void __launch_bounds__(Sage3Cfg<I8, HD>::THREADS, 1)
             const float m_prev = m_run;
 
             // ---- keys 64-127: read, free the columns for the next tile, max, exps (P_hi stays in registers)
-            ok = warp_wait(hi_full + t, j & 1, a.wait_ns, abort, kSpin);
+            ok = warp_wait(hi_full + t, j & 1, a.wait_ns, abort);
             if (!ok) break;
             tc_fence_after();
             uint32_t r[2][32];
@@ -356,7 +353,7 @@ __global__ void __launch_bounds__(Sage3Cfg<I8, HD>::THREADS, 1)
             ++turns;
 
             // ---- keys 0-63: read (after P(j-1).V_{j-1}), max, and where the max moves, scale P_hi down
-            ok = warp_wait(lo_full + t, j & 1, a.wait_ns, abort, kSpin);
+            ok = warp_wait(lo_full + t, j & 1, a.wait_ns, abort);
             if (!ok) break;
             tc_fence_after();
             tmem_ld32(t_lane + colS, r[0]);
