@@ -640,7 +640,7 @@ def rope_prepass_leg(dev, qkv, S, h, D, peaks, max_over_ranks, barrier, rot=96) 
         return max_over_ranks(e0.elapsed_time(e1)) / n
 
     ms_sep, ms_fused = timed(separate), timed(fused)
-    return {"kernels": "rms_rope_staged (q, k) + kmean_tma (priority stream) || quant_rows (q), then quant_rows (k)", "S": S, "heads": h,
+    return {"kernels": "fused: rms_rope_staged (k), then kmean_tma (priority stream) || rms_rope_staged (q) + quant_rows (q), then quant_rows (k)", "S": S, "heads": h,
             "rot_dim": rot, "ms_rms_rope_then_prepass": ms_sep, "ms_fused": ms_fused}
 
 

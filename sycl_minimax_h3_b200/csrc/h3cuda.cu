@@ -235,8 +235,9 @@ struct RopeArgs {
 };
 
 // ---- the Sage pre-pass (kernels/h3sycl.cpp:1733-1761) --------------------------------------------------------------
-// With rope: q and k are first normalised and rotated in place by the rms_rope kernel, as two h3s_rms_rope calls would
-// (the same bits), before the K mean forks off. (A single pass that normalises q inside its quantiser, saving one read
+// With rope: q and k are normalised and rotated in place by the rms_rope kernel, as two h3s_rms_rope calls would (the
+// same bits): k first, since the K mean needs it, then q on the main stream while the K mean runs beside it (measured
+// at configs[3]: 0.63 against 0.70 ms for the step with both rotations before the fork). (A single pass that normalises q inside its quantiser, saving one read
 // of q, measured slower at configs[3]: its rotation is compute-bound and, running beside the K mean, slows the K mean's
 // chains, the pre-pass's critical path; the quantiser that runs there now is memory-bound.)
 template <int DT>
@@ -249,15 +250,10 @@ int prepass_dt(Ctx& c, const void* q, const void* k, int64_t S, int64_t H, int64
     const int C = (int) (H * D);
     const int es = DtInfo<DT>::ES;
     cudaError_t e;
-    if (rope) {
-        if ((e = launch_rms_rope<DT>(const_cast<void*>(q), S, (int) H, (int) D, stride, rope->wq, rope->eps, rope->cs,
-                                     rope->rot, c.st)) != cudaSuccess)
-            return cuda_fail("rms_rope q", e);
-        if ((e = launch_rms_rope<DT>(const_cast<void*>(k), S, (int) H, (int) D, stride, rope->wk, rope->eps, rope->cs,
-                                     rope->rot, c.st)) != cudaSuccess)
-            return cuda_fail("rms_rope k", e);
-    }
-    // fork: the K mean runs on the aux stream beside the Q quantiser
+    if (rope && (e = launch_rms_rope<DT>(const_cast<void*>(k), S, (int) H, (int) D, stride, rope->wk, rope->eps,
+                                         rope->cs, rope->rot, c.st)) != cudaSuccess)
+        return cuda_fail("rms_rope k", e);
+    // fork: the K mean runs on the aux stream beside q's rotation and the Q quantiser
     if ((e = cudaEventRecord(c.ev_fork, c.st)) != cudaSuccess) return cuda_fail("event", e);
     if ((e = cudaStreamWaitEvent(c.aux, c.ev_fork, 0)) != cudaSuccess) return cuda_fail("event", e);
     if ((e = launch_kmean<DT>(k, S, C, stride, kmean, c.err, c.wait_ns, c.aux)) != cudaSuccess) return cuda_fail("kmean", e);
@@ -276,6 +272,9 @@ int prepass_dt(Ctx& c, const void* q, const void* k, int64_t S, int64_t H, int64
         }
         return cudaGetLastError();
     };
+    if (rope && (e = launch_rms_rope<DT>(const_cast<void*>(q), S, (int) H, (int) D, stride, rope->wq, rope->eps,
+                                         rope->cs, rope->rot, c.st)) != cudaSuccess)
+        return cuda_fail("rms_rope q", e);
     if ((e = quant(q, nullptr, iq, qs, vq)) != cudaSuccess) return cuda_fail("quantise q", e);
     if ((e = cudaStreamWaitEvent(c.st, c.ev_join, 0)) != cudaSuccess) return cuda_fail("event", e);
     if ((e = quant(k, kmean, ik, ks, vk)) != cudaSuccess) return cuda_fail("quantise k", e);
