@@ -3,7 +3,7 @@
 //   kmean     kmean[h*D+d] = (((0 + k_0) + k_1) + ... + k_{S-1}) / (float) S: one fp32 chain per channel in token order
 //             (the reference's loop, kernels/h3sycl.cpp:1733-1737). A chain cannot be split without changing its bits,
 //             so the work is shaped around it: a TMA ring streams 256-token x 64-channel tiles of k into shared memory
-//             (96 KB in flight per CTA) while 64 threads run the 64 chains over each tile, adding the 16-bit values
+//             (160 KB in flight per CTA) while 64 threads run the 64 chains over each tile, adding the 16-bit values
 //             with the mixed-precision add (no separate conversion).
 //   quant     per (head, 64-row block): m = max|x - mean|, inv = m > 0 ? 127/m : 0, scale = m/127,
 //             q = clamp(round(x * inv), -127, 127), round half away from zero (kernels/h3sycl.cpp:1738-1761).
@@ -63,7 +63,10 @@ __device__ __forceinline__ void ld16(const void* p, float* out) {
 
 // ---- K mean, TMA ring ----------------------------------------------------------------------------------------------
 constexpr int kMeanCh = 64;          // channels per CTA: 128-byte rows of 16-bit k per token, two chain warps
-constexpr int kMeanRingBytes = 96 * 1024;
+// The TMA ring of one K-mean CTA: 5 tiles of 32 KB. Beside the q quantiser, whose traffic lengthens the loads' latency,
+// a chain drained 3 tiles before the next arrived: measured at configs[3], the K mean beside the q quantiser took
+// 214.8 us with 96 KB, 196 us with 160 or 192 KB (167 us alone with any), the pre-pass 331 against 310.5 us.
+constexpr int kMeanRingBytes = 160 * 1024;
 constexpr int kMeanThreads = 32 + kMeanCh;   // warp 0: producer; warps 1-2: one thread per chain
 
 template <int DT>
